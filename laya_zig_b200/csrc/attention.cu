@@ -1,0 +1,258 @@
+// attention.cu -- bidirectional multi-head attention over packed sequences.
+//
+// Replaces attWorker (src/main.zig:2431-2489): per query row i and head h,
+// softmax(q_i . k_j / 8) over j in [klo, khi) -- all keys of the sequence on
+// global layers, |i - j| <= 64 on sliding layers -- then the weighted sum of
+// v_j. Here one CTA takes 64 query rows of one head of one sequence; four
+// warps hold 16 rows each. Scores and P.V run on the tensor cores
+// (mma.sync m16n8k16, f32 accumulate); the softmax is the online
+// (running max / running sum) form in f32 with exp2, normalised once at the
+// end as the reference does (2479-2486). Key/value tiles of 64 keys are
+// double-buffered in swizzled shared memory with cp.async.
+//
+// Inputs come straight from the QKV projection's output: row r of `qkv`
+// holds q | k | v (each 12 heads x 64, RoPE already applied to q and k),
+// which is the reference's split layout (splitJob 2626-2634).
+#include "attention.cuh"
+
+namespace laya {
+namespace {
+
+constexpr int QB = 64;   // query rows per CTA
+constexpr int KB = 64;   // keys per tile
+constexpr int THREADS = 128;
+
+// element offset of (row, col) in a 64x64 16-bit tile whose 16-byte chunks
+// are XOR-swizzled by row, so ldmatrix row fetches never share a bank.
+__device__ __forceinline__ int swz(int r, int c) { return r * 64 + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7); }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+    const int sz = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(sz) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Copy rows [r0, r0+64) x cols [c0, c0+64) of the [*, ld] matrix at `src`
+// into a swizzled tile; rows at or past `rend` are zero-filled.
+template <typename T>
+__device__ __forceinline__ void load_tile(T* tile, const T* src, int ld, int r0, int rend, int c0) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int ch = threadIdx.x + i * THREADS;
+        const int r = ch >> 3, cc = (ch & 7) * 8;
+        const bool valid = r0 + r < rend;
+        const T* s = src + (size_t)(valid ? r0 + r : r0) * ld + c0 + cc;
+        cp_async16(tile + swz(r, cc), s, valid);
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS) attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
+                                                            const int* __restrict__ cu_seqlens, int window) {
+    __shared__ __align__(128) T sQ[QB * 64];
+    __shared__ __align__(128) T sK[2][KB * 64];
+    __shared__ __align__(128) T sV[2][KB * 64];
+
+    const int seq = blockIdx.z, h = blockIdx.y;
+    const int start = cu_seqlens[seq];
+    const int L = cu_seqlens[seq + 1] - start;
+    const int q0 = blockIdx.x * QB;
+    if (q0 >= L) return;
+    const int ld = 3 * D;
+    const T* base = qkv + (size_t)start * ld;
+
+    int klo = 0, khi = L;
+    if (window >= 0) {
+        klo = max(0, q0 - window);
+        khi = min(L, q0 + QB - 1 + window + 1);
+    }
+    const int kt0 = klo / KB, kt1 = (khi + KB - 1) / KB;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    load_tile(sQ, base, ld, q0, L, h * HD);
+    load_tile(sK[0], base, ld, kt0 * KB, L, D + h * HD);
+    load_tile(sV[0], base, ld, kt0 * KB, L, 2 * D + h * HD);
+    cp_commit();
+
+    const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+    const int qi0 = q0 + warp * 16 + (lane >> 2), qi1 = qi0 + 8;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    uint32_t qa[4][4];
+
+    for (int kt = kt0; kt < kt1; kt++) {
+        const int buf = (kt - kt0) & 1;
+        if (kt + 1 < kt1) {
+            load_tile(sK[buf ^ 1], base, ld, (kt + 1) * KB, L, D + h * HD);
+            load_tile(sV[buf ^ 1], base, ld, (kt + 1) * KB, L, 2 * D + h * HD);
+        }
+        cp_commit();
+        cp_wait<1>();
+        __syncthreads();
+        if (kt == kt0) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                const int r = warp * 16 + (lane & 15), c = ks * 16 + (lane >> 4) * 8;
+                ldsm_x4(qa[ks], sQ + swz(r, c));
+            }
+        }
+        // S = Q K^T for 64 keys: 8 n-tiles of 8 keys
+        float s[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        const T* K = sK[buf];
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+#pragma unroll
+            for (int np = 0; np < 4; np++) {
+                uint32_t b[4];
+                const int mi = lane >> 3;
+                const int r = np * 16 + (lane & 7) + (mi >> 1) * 8, c = ks * 16 + (mi & 1) * 8;
+                ldsm_x4(b, K + swz(r, c));
+                mma16816<T>(s[2 * np], qa[ks], b[0], b[1]);
+                mma16816<T>(s[2 * np + 1], qa[ks], b[2], b[3]);
+            }
+        }
+        // mask + online softmax (two rows per thread: qi0 and qi1)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int kj = kt * KB + j * 8 + 2 * (lane & 3) + e;
+                const bool ok0 = kj < L && (window < 0 || abs(qi0 - kj) <= window);
+                const bool ok1 = kj < L && (window < 0 || abs(qi1 - kj) <= window);
+                s[j][e] = ok0 ? s[j][e] * sl2 : -INFINITY;
+                s[j][2 + e] = ok1 ? s[j][2 + e] * sl2 : -INFINITY;
+                mx0 = fmaxf(mx0, s[j][e]);
+                mx1 = fmaxf(mx1, s[j][2 + e]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float u0 = n0 == -INFINITY ? 0.f : n0, u1 = n1 == -INFINITY ? 0.f : n1;
+        const float a0 = exp2f(m0 - u0), a1 = exp2f(m1 - u1);
+        m0 = n0;
+        m1 = n1;
+        float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            s[j][0] = exp2f(s[j][0] - u0);
+            s[j][1] = exp2f(s[j][1] - u0);
+            s[j][2] = exp2f(s[j][2] - u1);
+            s[j][3] = exp2f(s[j][3] - u1);
+            rs0 += s[j][0] + s[j][1];
+            rs1 += s[j][2] + s[j][3];
+        }
+        l0 = l0 * a0 + rs0;
+        l1 = l1 * a1 + rs1;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            o[j][0] *= a0;
+            o[j][1] *= a0;
+            o[j][2] *= a1;
+            o[j][3] *= a1;
+        }
+        // O += P V: P as the A operand straight from the score registers
+        const T* V = sV[buf];
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            uint32_t pa[4];
+            pa[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int dp = 0; dp < 4; dp++) {
+                uint32_t b[4];
+                const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, c = dp * 16 + (lane >> 4) * 8;
+                ldsm_x4_t(b, V + swz(r, c));
+                mma16816<T>(o[2 * dp], pa, b[0], b[1]);
+                mma16816<T>(o[2 * dp + 1], pa, b[2], b[3]);
+            }
+        }
+        __syncthreads();
+    }
+
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+    T* dst = out + (size_t)start * D + h * HD + 2 * (lane & 3);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (qi0 < L) *reinterpret_cast<uint32_t*>(dst + (size_t)qi0 * D + j * 8) = pack2<T>(o[j][0] * i0, o[j][1] * i0);
+        if (qi1 < L) *reinterpret_cast<uint32_t*>(dst + (size_t)qi1 * D + j * 8) = pack2<T>(o[j][2] * i1, o[j][3] * i1);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* cu_seqlens, int n_seqs, int max_len,
+                             int window, cudaStream_t stream) {
+    if (n_seqs <= 0 || max_len <= 0) return cudaSuccess;
+    dim3 grid((max_len + QB - 1) / QB, H, n_seqs);
+    if (bf16)
+        attention_kernel<__nv_bfloat16><<<grid, THREADS, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, window);
+    else
+        attention_kernel<__half><<<grid, THREADS, 0, stream>>>(static_cast<const __half*>(qkv),
+                                                               static_cast<__half*>(out), cu_seqlens, window);
+    return cudaGetLastError();
+}
+
+}  // namespace laya

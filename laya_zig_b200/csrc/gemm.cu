@@ -1,0 +1,420 @@
+// gemm.cu -- persistent tcgen05 GEMM for the projection layers.
+//
+// One CTA per SM, 192 threads, warp-specialised:
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per
+//               k-block into a STAGES-deep shared-memory ring (128B swizzle).
+//   warp 1      allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
+//               K=16) into a double-buffered f32 accumulator in TMEM and
+//               commits to mbarriers (ring slot free / accumulator full).
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp owns the
+//               32 TMEM lanes = tile rows its warp id allows), the fused
+//               elementwise op of the layer, 16-byte global stores.
+// The accumulator is double-buffered, so the epilogue of tile i overlaps the
+// MMAs of tile i+1. Every wait is bounded (common.cuh); a CTA that gives up
+// records the error, drains its own TMA loads and MMAs, frees TMEM and exits.
+//
+// Numerics: inputs are 16-bit, products are exact in f32 and accumulate in
+// f32, as the reference's f32 FMA chains over f16-widened weights do
+// (src/main.zig:934-974); only the rounding of the activations to 16 bits
+// and the summation order differ.
+#include <cstdio>
+
+#include "gemm.cuh"
+
+namespace laya {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int NUM_THREADS = 192;
+
+template <int BN>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int TMEM_COLS = 2 * BN;  // two accumulators of BN f32 columns
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <typename T>
+struct Pack;
+template <>
+struct Pack<__nv_bfloat16> {
+    static __device__ __forceinline__ uint32_t two(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+template <>
+struct Pack<__half> {
+    static __device__ __forceinline__ uint32_t two(float a, float b) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+
+// 32 consecutive f32 columns of this thread's row.
+__device__ __forceinline__ void load_cols(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    tmem_ld32(taddr, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store16x32(T* dst, const float (&v)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        uint4 u;
+        u.x = Pack<T>::two(v[8 * q + 0], v[8 * q + 1]);
+        u.y = Pack<T>::two(v[8 * q + 2], v[8 * q + 3]);
+        u.z = Pack<T>::two(v[8 * q + 4], v[8 * q + 5]);
+        u.w = Pack<T>::two(v[8 * q + 6], v[8 * q + 7]);
+        d[q] = u;
+    }
+}
+
+__device__ __forceinline__ void add_bias(float (&v)[32], const float* bias, int col) {
+    if (bias) {
+        const float4* b = reinterpret_cast<const float4*>(bias + col);
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const float4 t = __ldg(b + q);
+            v[4 * q] += t.x;
+            v[4 * q + 1] += t.y;
+            v[4 * q + 2] += t.z;
+            v[4 * q + 3] += t.w;
+        }
+    }
+}
+
+template <int BN, int EPI, typename T>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tacc, int row, int n_blk) {
+    const bool live = row < a.M;
+    if constexpr (EPI == EPI_GLU) {
+        // columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows
+        constexpr int HALF = BN / 2;
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+            float g[32], u[32];
+            load_cols(tacc + c, g);
+            load_cols(tacc + HALF + c, u);
+            if (live) {
+#pragma unroll
+                for (int i = 0; i < 32; i++) g[i] = gelu_as(g[i]) * u[i];
+                store16x32<T>(reinterpret_cast<T*>(a.out16) + (size_t)row * a.ldo + n_blk * HALF + c, g);
+            }
+        }
+    } else if constexpr (EPI == EPI_QKV) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+            float x0[32], x1[32];
+            load_cols(tacc + c, x0);
+            load_cols(tacc + c + 32, x1);
+            const int col = n_blk * BN + c;
+            if (live) {
+                add_bias(x0, a.bias, col);
+                add_bias(x1, a.bias, col + 32);
+                if (col < a.rope_cols) {
+                    // rotate_half pairing (d, d+32) within the head, src/main.zig:2512-2519
+                    const float4* cs = reinterpret_cast<const float4*>(a.rope + (size_t)a.pos[row] * 32);
+#pragma unroll
+                    for (int d = 0; d < 32; d += 2) {
+                        const float4 t = __ldg(cs + d / 2);  // (cos d, sin d, cos d+1, sin d+1)
+                        const float a0 = x0[d], b0 = x1[d], a1 = x0[d + 1], b1 = x1[d + 1];
+                        x0[d] = a0 * t.x - b0 * t.y;
+                        x1[d] = b0 * t.x + a0 * t.y;
+                        x0[d + 1] = a1 * t.z - b1 * t.w;
+                        x1[d + 1] = b1 * t.z + a1 * t.w;
+                    }
+                }
+                T* dst = reinterpret_cast<T*>(a.out16) + (size_t)row * a.ldo + col;
+                store16x32<T>(dst, x0);
+                store16x32<T>(dst + 32, x1);
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            load_cols(tacc + c, v);
+            const int col = n_blk * BN + c;
+            if (!live) continue;
+            add_bias(v, a.bias, col);
+            if constexpr (EPI == EPI_F32 || EPI == EPI_RESID) {
+                float4* dst = reinterpret_cast<float4*>(a.out_f32 + (size_t)row * a.ldo + col);
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    if constexpr (EPI == EPI_RESID) {
+                        const float4 r = dst[q];
+                        o.x += r.x;
+                        o.y += r.y;
+                        o.z += r.z;
+                        o.w += r.w;
+                    }
+                    dst[q] = o;
+                }
+            } else {
+                if constexpr (EPI == EPI_RELU) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = fmaxf(v[i], 0.0f);
+                }
+                store16x32<T>(reinterpret_cast<T*>(a.out16) + (size_t)row * a.ldo + col, v);
+            }
+        }
+    }
+}
+
+template <int BN, int EPI, typename T>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map, GemmArgs args) {
+    using C = Cfg<BN>;
+    constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t* empty = full + C::STAGES;
+    uint64_t* tfull = empty + C::STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tiles_m = (args.M + BM - 1) / BM;
+    const int tiles_n = args.N / BN;
+    const int total = tiles_m * tiles_n;
+    const int nk = args.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        fence_proxy_async();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&a_map);
+        prefetch_tmap(&b_map);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued_phase[C::STAGES];
+            for (int s = 0; s < C::STAGES; s++) issued_phase[s] = -1;
+            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+                for (int kb = 0; kb < nk; kb++) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, args.err, abort_flag)) goto producer_done;
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tma_load_2d(sa, &a_map, &full[stage], kb * BK, m0);
+                    tma_load_2d(sa + C::A_BYTES, &b_map, &full[stage], kb * BK, n0);
+                    issued_phase[stage] = (int)phase;
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        producer_done:
+            // Let every load this thread issued land before shared memory goes away.
+            for (int s = 0; s < C::STAGES; s++) {
+                if (issued_phase[s] < 0) continue;
+                const unsigned long long t0 = globaltimer();
+                while (!mbar_try_wait(&full[s], (uint32_t)issued_phase[s])) {
+                    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+                        atomicOr(args.err, ERR_WAIT_TIMEOUT);
+                        break;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int it = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
+                const int buf = it & 1;
+                const uint32_t tph = (it >> 1) & 1;
+                if (!mbar_wait(&tempty[buf], tph ^ 1, args.err, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + buf * BN;
+                bool ok = true;
+                for (int kb = 0; kb < nk; kb++) {
+                    if (!mbar_wait(&full[stage], phase, args.err, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+                    const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + C::A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++)
+                        tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
+                    tc_commit(&empty[stage]);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[buf]);
+            }
+            // All MMAs this thread issued are complete once `drain` flips.
+            tc_commit(drain);
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try_wait(drain, 0)) {
+                if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+                    atomicOr(args.err, ERR_WAIT_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int it = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
+            const int buf = it & 1;
+            const uint32_t tph = (it >> 1) & 1;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&tfull[buf], tph, args.err, abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const int row = (t / tiles_n) * BM + q * 32 + lane;
+            const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+            epilogue_tile<BN, EPI, T>(args, tacc, row, t % tiles_n);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+template <int BN, int EPI, typename T>
+cudaError_t prepare_one() {
+    return cudaFuncSetAttribute(gemm_kernel<BN, EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+}
+
+template <int BN, typename T>
+cudaError_t prepare_bn() {
+    cudaError_t e = cudaSuccess;
+    if (e == cudaSuccess) e = prepare_one<BN, EPI_F32, T>();
+    if (e == cudaSuccess) e = prepare_one<BN, EPI_ACT16, T>();
+    if (e == cudaSuccess) e = prepare_one<BN, EPI_QKV, T>();
+    if (e == cudaSuccess) e = prepare_one<BN, EPI_RESID, T>();
+    if (e == cudaSuccess) e = prepare_one<BN, EPI_GLU, T>();
+    if (e == cudaSuccess) e = prepare_one<BN, EPI_RELU, T>();
+    return e;
+}
+
+template <int BN, int EPI, typename T>
+cudaError_t launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const GemmArgs& args, int num_sms,
+                       cudaStream_t stream) {
+    using C = Cfg<BN>;
+    const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    if (grid <= 0) return cudaSuccess;
+    gemm_kernel<BN, EPI, T><<<grid, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, args);
+    return cudaGetLastError();
+}
+
+template <int BN, typename T>
+cudaError_t dispatch_epi(int epi, const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int sms,
+                         cudaStream_t s) {
+    switch (epi) {
+        case EPI_F32: return launch_one<BN, EPI_F32, T>(a, b, args, sms, s);
+        case EPI_ACT16: return launch_one<BN, EPI_ACT16, T>(a, b, args, sms, s);
+        case EPI_QKV: return launch_one<BN, EPI_QKV, T>(a, b, args, sms, s);
+        case EPI_RESID: return launch_one<BN, EPI_RESID, T>(a, b, args, sms, s);
+        case EPI_GLU: return launch_one<BN, EPI_GLU, T>(a, b, args, sms, s);
+        case EPI_RELU: return launch_one<BN, EPI_RELU, T>(a, b, args, sms, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+CUresult make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
+                      bool bf16) {
+    using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static EncodeFn encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return CUDA_ERROR_NOT_FOUND;
+        encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {inner * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+cudaError_t gemm_prepare() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static unsigned long long done = 0;  // one bit per device
+    if (dev < 64 && (done >> dev) & 1ull) return cudaSuccess;
+    if (e == cudaSuccess) e = prepare_bn<256, __nv_bfloat16>();
+    if (e == cudaSuccess) e = prepare_bn<256, __half>();
+    if (e == cudaSuccess) e = prepare_bn<128, __nv_bfloat16>();
+    if (e == cudaSuccess) e = prepare_bn<128, __half>();
+    if (e == cudaSuccess && dev < 64) done |= 1ull << dev;
+    return e;
+}
+
+cudaError_t launch_gemm(int epi, int bn, bool bf16, const CUtensorMap& a_map, const CUtensorMap& b_map,
+                        const GemmArgs& args, int num_sms, cudaStream_t stream) {
+    if (args.K % BK || args.N % bn || args.M < 0) return cudaErrorInvalidValue;
+    if (bn == 256)
+        return bf16 ? dispatch_epi<256, __nv_bfloat16>(epi, a_map, b_map, args, num_sms, stream)
+                    : dispatch_epi<256, __half>(epi, a_map, b_map, args, num_sms, stream);
+    if (bn == 128)
+        return bf16 ? dispatch_epi<128, __nv_bfloat16>(epi, a_map, b_map, args, num_sms, stream)
+                    : dispatch_epi<128, __half>(epi, a_map, b_map, args, num_sms, stream);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace laya

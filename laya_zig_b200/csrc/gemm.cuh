@@ -1,0 +1,47 @@
+// gemm.cuh -- tcgen05 projection GEMM with fused epilogues (declarations).
+//
+// out = A[M,K] * B[N,K]^T, A and B 16-bit (bf16 or f16) K-major, f32
+// accumulation in TMEM. Replaces the reference's linear16/packed kernel
+// (src/main.zig:844-1099) and fuses the elementwise job that follows each
+// projection in `forward` (src/main.zig:2641-2754).
+#pragma once
+#include "common.cuh"
+
+namespace laya {
+
+enum Epilogue : int {
+    EPI_F32 = 0,    // out_f32 = acc (+ bias)                          plain GEMM
+    EPI_ACT16 = 1,  // out16 = acc (+ bias)                           plain GEMM
+    EPI_QKV = 2,    // out16 = rope(acc (+ bias)) on q,k columns        splitJob+ropeJob (2626-2634, 2496-2521)
+    EPI_RESID = 3,  // out_f32 += acc (+ bias)                          addResJob (2571-2578), biasJob (1073-1079)
+    EPI_GLU = 4,    // out16[j] = gelu(acc[gate j]) * acc[up j]         mlpJob (2557-2569)
+    EPI_RELU = 5,   // out16 = relu(acc + bias)                         reluJob (2580-2586)
+};
+
+struct GemmArgs {
+    int M, N, K;
+    const float* bias;      // [N] or null
+    float* out_f32;         // EPI_F32 / EPI_RESID
+    void* out16;            // 16-bit outputs (type = the GEMM's element type)
+    int ldo;                // output row stride in elements
+    const int* pos;         // EPI_QKV: RoPE position of each row
+    const float2* rope;     // EPI_QKV: [MAX_POS][32] (cos, sin)
+    int rope_cols;          // EPI_QKV: RoPE applies to columns [0, rope_cols)
+    int* err;               // device error word
+};
+
+// 2-D tensor map over a row-major [rows][inner] 16-bit matrix, box
+// [box_rows][64] with 128-byte swizzle (the UMMA K-major SW128 layout).
+CUresult make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
+                      bool bf16);
+
+// Raise the dynamic shared-memory limit of every GEMM instantiation on the
+// current device (once per device; must not run during stream capture).
+cudaError_t gemm_prepare();
+
+// Launch one GEMM. BN (128 or 256) must divide N, 64 must divide K.
+// A's map has box rows 128, B's map box rows BN. Returns a CUDA error code.
+cudaError_t launch_gemm(int epi, int bn, bool bf16, const CUtensorMap& a_map, const CUtensorMap& b_map,
+                        const GemmArgs& args, int num_sms, cudaStream_t stream);
+
+}  // namespace laya

@@ -1,0 +1,36 @@
+// kernels.cuh -- launchers for the row-wise kernels (norm.cu, tail.cu, convert.cu).
+#pragma once
+#include "common.cuh"
+
+namespace laya {
+
+// norm.cu ------------------------------------------------------------------
+cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_seqs, int M, const void* emb,
+                         const float* w, float* x, void* xn, int* pos, int* seq_of, int* err, cudaStream_t s);
+cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, cudaStream_t s);
+cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const float* type_emb,
+                         const uint32_t* qtypes, const int* seq_of, const float* w1, const float* b1, int M,
+                         cudaStream_t s);
+
+// tail.cu ------------------------------------------------------------------
+struct TailWeights {
+    const float *s0w, *s0b, *s1w, *s1b, *s3w, *s3b;  // scorer: LN, 768x768 + b, 1x768 + b
+    const float *a0w, *a0b, *a2w, *a2b;              // act head: 256x772 + b, 2x256 + b
+};
+constexpr int SCORER_GROUPS = D / 64;  // partial sums per marker, one per 64 scorer outputs
+constexpr int MAX_MARKERS_PER_SEQ = 1024;
+
+// mv: [G][768] scratch, partial: [G][SCORER_GROUPS] scratch.
+cudaError_t launch_tail(const float* x, const int* cu_seqlens, const uint32_t* markers, const int* cu_markers,
+                        int n_seqs, int G, const TailWeights& w, float* mv, float* partial, float* logits,
+                        float* act, float* pooled, int* err, cudaStream_t s);
+
+// convert.cu ---------------------------------------------------------------
+// dst[r][c] (16-bit, bf16 or f16) <- src (F32 / F16 / BF16 tag) row perm(r);
+// glu_perm interleaves a [2*half][cols] gate|up matrix into tiles of
+// `tile` rows: tile/2 gate rows followed by the matching tile/2 up rows.
+cudaError_t launch_convert16(void* dst, bool dst_bf16, const void* src, int src_dtype, size_t rows, size_t cols,
+                             int glu_tile, cudaStream_t s);
+cudaError_t launch_convert_f32(float* dst, const void* src, int src_dtype, size_t n, cudaStream_t s);
+
+}  // namespace laya

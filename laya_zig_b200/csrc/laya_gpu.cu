@@ -1,0 +1,792 @@
+// laya_gpu.cu -- context, weight upload, forward driver and the C ABI.
+//
+// The forward pass is the reference's forward() (src/main.zig:2641-2817)
+// restructured for the GPU: all sequences of a batch are packed back to back
+// (varlen, no padding); every projection is one tcgen05 GEMM whose epilogue
+// performs the elementwise job that follows it; one CUDA graph per batch
+// shape replays the ~170 launches of a forward.
+//
+// Per encoder layer l (sliding = l % 3 != 0, main.zig:2366):
+//   [ln]       xn  = LN(x; attn_norm)          (layer 0: xn = x, main.zig:2660-2665)
+//   [gemm]     qkv = rope(xn Wqkv^T)           (2666-2671)
+//   [attn]     ctx = attention(qkv, window)    (2673-2684)
+//   [gemm]     x  += ctx Wo^T                  (2686-2688)
+//   [ln]       xn  = LN(x; mlp_norm)           (2691)
+//   [gemm]     g   = glu(xn Wi^T)              (2693-2695)
+//   [gemm]     x  += g Wo2^T                   (2697-2699)
+// then x = LN_final(x) + type_emb[qtype] with head norm1 fused (2708-2716),
+// the two head layers (2714-2754: biases, no RoPE, full attention, ReLU FFN),
+// and the tail (scorer, act head; 2756-2814).
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/laya_gpu.h"
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+using namespace laya;
+
+namespace {
+
+thread_local std::string g_create_error = "no error";
+
+struct EncW {
+    void *wqkv, *wo, *wi, *wo2;
+    float *attn_norm, *mlp_norm;
+    CUtensorMap m_qkv, m_wo, m_wi, m_wo2;
+};
+
+struct HeadW {
+    float *n1w, *n1b, *n2w, *n2b, *in_b, *out_b, *l1_b, *l2_b;
+    void *in_w, *out_w, *l1_w, *l2_w;
+    CUtensorMap m_in, m_out, m_l1, m_l2;
+};
+
+struct GraphKey {
+    int M, S, G, maxlen;
+    const void *ids, *cu, *mk, *cum, *qt, *lg, *act, *pooled, *hidden;
+    bool operator<(const GraphKey& o) const {
+        return std::tie(M, S, G, maxlen, ids, cu, mk, cum, qt, lg, act, pooled, hidden) <
+               std::tie(o.M, o.S, o.G, o.maxlen, o.ids, o.cu, o.mk, o.cum, o.qt, o.lg, o.act, o.pooled, o.hidden);
+    }
+};
+
+}  // namespace
+
+struct laya_ctx {
+    int device = 0;
+    bool bf16 = true;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    std::string err = "no error";
+    std::vector<void*> allocs;
+
+    // weights
+    void* emb = nullptr;
+    float *emb_norm = nullptr, *final_norm = nullptr, *type_emb = nullptr;
+    EncW enc[NL];
+    HeadW head[HEAD_LAYERS];
+    TailWeights tail{};
+    float2* rope = nullptr;
+
+    // workspace (capacities in tokens / sequences / markers)
+    int capM = 0, capS = 0, capG = 0;
+    std::vector<void*> ws;
+    float* x = nullptr;
+    void *xn = nullptr, *qkv = nullptr, *ctxb = nullptr, *mlp = nullptr, *ff = nullptr;
+    int *pos = nullptr, *seq_of = nullptr;
+    float *mv = nullptr, *partial = nullptr;
+    // staged batch inputs / outputs for the host-buffer entry points
+    uint32_t* d_ids = nullptr;
+    int* d_cu = nullptr;
+    uint32_t* d_qt = nullptr;
+    uint32_t* d_mk = nullptr;
+    int* d_cum = nullptr;
+    float *d_logits = nullptr, *d_act = nullptr, *d_pooled = nullptr;
+    CUtensorMap m_xn, m_ctx, m_mlp, m_ff;
+    int* d_err = nullptr;
+    int* h_err = nullptr;  // pinned
+    void* h_stage = nullptr;
+    size_t h_stage_bytes = 0;
+
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+};
+
+namespace {
+
+int fail(laya_ctx* c, int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (c) c->err = buf;
+    else g_create_error = buf;
+    return code;
+}
+
+#define CK(call)                                                                                      \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess)                                                                        \
+            return fail(c, e_ == cudaErrorMemoryAllocation ? LAYA_ERR_OOM : LAYA_ERR_CUDA, "%s: %s (%s:%d)", \
+                        #call, cudaGetErrorString(e_), __FILE__, __LINE__);                           \
+    } while (0)
+
+size_t elem_size(int dt) { return dt == LAYA_DT_F32 ? 4 : 2; }
+
+const laya_tensor* find(const laya_tensor* t, int n, const char* name) {
+    for (int i = 0; i < n; i++)
+        if (t[i].name && strcmp(t[i].name, name) == 0) return &t[i];
+    return nullptr;
+}
+
+int check_tensor(laya_ctx* c, const laya_tensor* t, int n, const char* name, uint64_t numel, const laya_tensor** out) {
+    const laya_tensor* e = find(t, n, name);
+    if (!e) return fail(c, LAYA_ERR_MISSING_TENSOR, "missing tensor: %s", name);
+    if (e->dtype != LAYA_DT_F32 && e->dtype != LAYA_DT_F16 && e->dtype != LAYA_DT_BF16)
+        return fail(c, LAYA_ERR_DTYPE, "tensor %s has dtype %d, expected F16, BF16 or F32", name, (int)e->dtype);
+    if (e->numel != numel)
+        return fail(c, LAYA_ERR_SHAPE, "tensor %s has %llu elements, expected %llu", name,
+                    (unsigned long long)e->numel, (unsigned long long)numel);
+    if (!e->data) return fail(c, LAYA_ERR_ARG, "tensor %s has no data", name);
+    *out = e;
+    return LAYA_OK;
+}
+
+int dev_alloc(laya_ctx* c, void** p, size_t bytes, std::vector<void*>& list) {
+    cudaError_t e = cudaMalloc(p, bytes < 256 ? 256 : bytes);
+    if (e != cudaSuccess) return fail(c, LAYA_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    list.push_back(*p);
+    return LAYA_OK;
+}
+
+// Upload one tensor through a device staging buffer; matrices -> 16-bit
+// (optionally GLU-interleaved), vectors -> f32.
+int upload(laya_ctx* c, const laya_tensor* t, int n, const char* name, uint64_t rows, uint64_t cols, bool matrix,
+           int glu_tile, void** dst, void* staging) {
+    const laya_tensor* e;
+    int rc = check_tensor(c, t, n, name, rows * cols, &e);
+    if (rc) return rc;
+    rc = dev_alloc(c, dst, rows * cols * (matrix ? 2 : 4), c->allocs);
+    if (rc) return rc;
+    CK(cudaMemcpy(staging, e->data, rows * cols * elem_size(e->dtype), cudaMemcpyHostToDevice));
+    if (matrix)
+        CK(launch_convert16(*dst, c->bf16, staging, e->dtype, rows, cols, glu_tile, c->stream));
+    else
+        CK(launch_convert_f32(static_cast<float*>(*dst), staging, e->dtype, rows * cols, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return LAYA_OK;
+}
+
+int weight_map(laya_ctx* c, CUtensorMap* m, const void* w, uint64_t rows, uint64_t cols) {
+    CUresult r = make_tmap_2d(m, w, cols, rows, 256, c->bf16);
+    if (r != CUDA_SUCCESS) return fail(c, LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return LAYA_OK;
+}
+
+void free_workspace(laya_ctx* c) {
+    for (auto& g : c->graphs) cudaGraphExecDestroy(g.second);
+    c->graphs.clear();
+    for (void* p : c->ws) cudaFree(p);
+    c->ws.clear();
+    c->capM = c->capS = c->capG = 0;
+}
+
+int ensure_workspace(laya_ctx* c, int M, int S, int G) {
+    if (M <= c->capM && S <= c->capS && G <= c->capG) return LAYA_OK;
+    const int nM = std::max(M, c->capM), nS = std::max(S, c->capS), nG = std::max(std::max(G, c->capG), 1);
+    CK(cudaStreamSynchronize(c->stream));
+    free_workspace(c);
+    const size_t e16 = 2;
+    int rc = 0;
+    auto A = [&](void** p, size_t bytes) { if (!rc) rc = dev_alloc(c, p, bytes, c->ws); };
+    A((void**)&c->x, (size_t)nM * D * 4);
+    A(&c->xn, (size_t)nM * D * e16);
+    A(&c->qkv, (size_t)nM * 3 * D * e16);
+    A(&c->ctxb, (size_t)nM * D * e16);
+    A(&c->mlp, (size_t)nM * INTER * e16);
+    A(&c->ff, (size_t)nM * HEAD_FF * e16);
+    A((void**)&c->pos, (size_t)nM * 4);
+    A((void**)&c->seq_of, (size_t)nM * 4);
+    A((void**)&c->mv, (size_t)nG * D * 4);
+    A((void**)&c->partial, (size_t)nG * SCORER_GROUPS * 4);
+    A((void**)&c->d_ids, (size_t)nM * 4);
+    A((void**)&c->d_cu, (size_t)(nS + 1) * 4);
+    A((void**)&c->d_qt, (size_t)nS * 4);
+    A((void**)&c->d_mk, (size_t)nG * 4);
+    A((void**)&c->d_cum, (size_t)(nS + 1) * 4);
+    A((void**)&c->d_logits, (size_t)nG * 4);
+    A((void**)&c->d_act, (size_t)nS * 2 * 4);
+    A((void**)&c->d_pooled, (size_t)nS * D * 4);
+    if (rc) {
+        free_workspace(c);
+        return rc;
+    }
+    c->capM = nM;
+    c->capS = nS;
+    c->capG = nG;
+    CUresult r = make_tmap_2d(&c->m_xn, c->xn, D, nM, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&c->m_ctx, c->ctxb, D, nM, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&c->m_mlp, c->mlp, INTER, nM, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&c->m_ff, c->ff, HEAD_FF, nM, 128, c->bf16);
+    if (r != CUDA_SUCCESS) return fail(c, LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    const size_t stage = (size_t)nM * 4 + (size_t)(nS + 1) * 8 + (size_t)nS * 4 + (size_t)nG * 4 + 64 +
+                         (size_t)nG * 4 + (size_t)nS * 8;
+    if (stage > c->h_stage_bytes) {
+        if (c->h_stage) cudaFreeHost(c->h_stage);
+        c->h_stage = nullptr;
+        CK(cudaMallocHost(&c->h_stage, stage));
+        c->h_stage_bytes = stage;
+    }
+    return LAYA_OK;
+}
+
+struct Batch {  // device pointers + host-side shape
+    const uint32_t* ids;
+    const int* cu;
+    const uint32_t* mk;
+    const int* cum;
+    const uint32_t* qt;
+    int S, M, G, maxlen;
+};
+
+struct Outs {
+    float *logits, *act, *pooled, *hidden;
+};
+
+cudaError_t gemm(laya_ctx* c, int epi, const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K,
+                 const float* bias, float* out_f32, void* out16, int ldo, int rope_cols, cudaStream_t s) {
+    GemmArgs g{};
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.out_f32 = out_f32;
+    g.out16 = out16;
+    g.ldo = ldo;
+    g.pos = c->pos;
+    g.rope = c->rope;
+    g.rope_cols = rope_cols;
+    g.err = c->d_err;
+    return launch_gemm(epi, 256, c->bf16, a, b, g, c->num_sms, s);
+}
+
+// The whole forward on stream `s`. The hook sees begin(stage)/end(stage)
+// around every kernel launch and tap(tag) after each --dumpstats point.
+template <typename Hook>
+cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t s, Hook& hook) {
+    cudaError_t e;
+#define RUN(stage, x)                           \
+    do {                                        \
+        hook.begin(stage);                      \
+        e = (x);                                \
+        hook.end(stage);                        \
+        if (e != cudaSuccess) return e;         \
+    } while (0)
+    const int M = b.M;
+    RUN(LAYA_STAGE_EMBED,
+        launch_embed(c->bf16, b.ids, b.cu, b.S, M, c->emb, c->emb_norm, c->x, c->xn, c->pos, c->seq_of, c->d_err, s));
+    hook.tap(0);
+    for (int l = 0; l < NL; l++) {
+        const EncW& w = c->enc[l];
+        if (w.attn_norm) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.attn_norm, nullptr, M, s));
+        RUN(LAYA_STAGE_GEMM_QKV,
+            gemm(c, EPI_QKV, c->m_xn, w.m_qkv, M, 3 * D, D, nullptr, nullptr, c->qkv, 3 * D, 2 * D, s));
+        RUN(LAYA_STAGE_ATTN,
+            launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, (l % 3) ? WINDOW : -1, s));
+        RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, c->m_ctx, w.m_wo, M, D, D, nullptr, c->x, nullptr, D, 0, s));
+        RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.mlp_norm, nullptr, M, s));
+        RUN(LAYA_STAGE_GEMM_UP,
+            gemm(c, EPI_GLU, c->m_xn, w.m_wi, M, 2 * INTER, D, nullptr, nullptr, c->mlp, INTER, 0, s));
+        RUN(LAYA_STAGE_GEMM_DOWN, gemm(c, EPI_RESID, c->m_mlp, w.m_wo2, M, D, INTER, nullptr, c->x, nullptr, D, 0, s));
+        hook.tap(1 + l);
+    }
+    RUN(LAYA_STAGE_FINAL, launch_final(c->bf16, c->x, c->xn, c->final_norm, c->type_emb, b.qt, c->seq_of,
+                                       c->head[0].n1w, c->head[0].n1b, M, s));
+    hook.tap(24);
+    for (int l = 0; l < HEAD_LAYERS; l++) {
+        const HeadW& w = c->head[l];
+        if (l > 0) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n1w, w.n1b, M, s));
+        RUN(LAYA_STAGE_GEMM_QKV, gemm(c, EPI_QKV, c->m_xn, w.m_in, M, 3 * D, D, w.in_b, nullptr, c->qkv, 3 * D, 0, s));
+        RUN(LAYA_STAGE_ATTN, launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, -1, s));
+        RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, c->m_ctx, w.m_out, M, D, D, w.out_b, c->x, nullptr, D, 0, s));
+        RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n2w, w.n2b, M, s));
+        RUN(LAYA_STAGE_GEMM_UP,
+            gemm(c, EPI_RELU, c->m_xn, w.m_l1, M, HEAD_FF, D, w.l1_b, nullptr, c->ff, HEAD_FF, 0, s));
+        RUN(LAYA_STAGE_GEMM_DOWN,
+            gemm(c, EPI_RESID, c->m_ff, w.m_l2, M, D, HEAD_FF, w.l2_b, c->x, nullptr, D, 0, s));
+        hook.tap(25 + l);
+    }
+    RUN(LAYA_STAGE_TAIL, launch_tail(c->x, b.cu, b.mk, b.cum, b.S, b.G, c->tail, c->mv, c->partial, o.logits, o.act,
+                                     o.pooled ? o.pooled : c->d_pooled, c->d_err, s));
+    hook.extra(LAYA_STAGE_TAIL, b.G > 0 ? 2 : 0);  // launch_tail issues 3 kernels when there are markers
+    if (o.hidden) {
+        e = cudaMemcpyAsync(o.hidden, c->x, (size_t)M * D * 4, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+#undef RUN
+}
+
+struct NoHook {
+    void begin(int) {}
+    void end(int) {}
+    void tap(int) {}
+    void extra(int, int) {}
+};
+
+// Copies x to the host after every --dumpstats point.
+struct TraceHook {
+    laya_ctx* c;
+    float* trace;
+    size_t LD;
+    void begin(int) {}
+    void end(int) {}
+    void extra(int, int) {}
+    void tap(int tag) { cudaMemcpyAsync(trace + (size_t)tag * LD, c->x, LD * 4, cudaMemcpyDeviceToHost, c->stream); }
+};
+
+// An event pair around every launch; per-stage times summed after a sync.
+struct ProfileHook {
+    cudaStream_t s;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> stage;
+    size_t used = 0;
+    int launches[LAYA_N_STAGES] = {0};
+    void begin(int st) {
+        if (used + 2 > ev.size()) {
+            cudaEvent_t a, b;
+            cudaEventCreate(&a);
+            cudaEventCreate(&b);
+            ev.push_back(a);
+            ev.push_back(b);
+            stage.push_back(st);
+        }
+        stage[used / 2] = st;
+        cudaEventRecord(ev[used], s);
+    }
+    void end(int st) {
+        cudaEventRecord(ev[used + 1], s);
+        used += 2;
+        launches[st]++;
+    }
+    void tap(int) {}
+    void extra(int st, int n) { launches[st] += n; }
+    void collect(float* stage_ms) {
+        for (size_t i = 0; i < used; i += 2) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            stage_ms[stage[i / 2]] += ms;
+        }
+        used = 0;
+    }
+    ~ProfileHook() {
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    }
+};
+
+// Run (capturing a graph on first use of this shape) on stream s.
+int launch_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t s) {
+    GraphKey k{b.M, b.S, b.G, b.maxlen, b.ids, b.cu, b.mk, b.cum, b.qt, o.logits, o.act, o.pooled, o.hidden};
+    auto it = c->graphs.find(k);
+    if (it == c->graphs.end()) {
+        if (c->graphs.size() >= 16) {
+            for (auto& g : c->graphs) cudaGraphExecDestroy(g.second);
+            c->graphs.clear();
+        }
+        cudaGraph_t graph;
+        CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        NoHook hook;
+        cudaError_t e = run_forward(c, b, o, s, hook);
+        cudaError_t e2 = cudaStreamEndCapture(s, &graph);
+        if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "launch during capture: %s", cudaGetErrorString(e));
+        if (e2 != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(e2));
+        cudaGraphExec_t exec;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+        it = c->graphs.emplace(k, exec).first;
+    }
+    CK(cudaGraphLaunch(it->second, s));
+    return LAYA_OK;
+}
+
+int check_seqs(laya_ctx* c, const laya_seq* seqs, uint32_t n, int* M, int* G, int* maxlen) {
+    long long m = 0, g = 0;
+    int ml = 0;
+    for (uint32_t s = 0; s < n; s++) {
+        const laya_seq& q = seqs[s];
+        if (q.len == 0 || q.len > LAYA_MAX_LEN)
+            return fail(c, LAYA_ERR_ARG, "sequence %u: length %u outside [1, %d]", s, q.len, LAYA_MAX_LEN);
+        if (!q.ids) return fail(c, LAYA_ERR_ARG, "sequence %u: ids is NULL", s);
+        if (q.qtype > 2) return fail(c, LAYA_ERR_ARG, "sequence %u: qtype %u (expected 0, 1 or 2)", s, q.qtype);
+        if (q.n_markers > LAYA_MAX_MARKERS)
+            return fail(c, LAYA_ERR_ARG, "sequence %u: %u markers (max %d)", s, q.n_markers, LAYA_MAX_MARKERS);
+        if (q.n_markers && !q.markers) return fail(c, LAYA_ERR_ARG, "sequence %u: markers is NULL", s);
+        for (uint32_t i = 0; i < q.len; i++)
+            if (q.ids[i] >= (uint32_t)LAYA_VOCAB)
+                return fail(c, LAYA_ERR_ARG, "sequence %u: token %u has id %u >= vocab %d", s, i, q.ids[i], LAYA_VOCAB);
+        for (uint32_t r = 0; r < q.n_markers; r++)
+            if (q.markers[r] >= q.len)
+                return fail(c, LAYA_ERR_ARG, "sequence %u: marker %u at %u >= length %u", s, r, q.markers[r], q.len);
+        m += q.len;
+        g += q.n_markers;
+        ml = std::max(ml, (int)q.len);
+    }
+    if (m > (1LL << 30)) return fail(c, LAYA_ERR_ARG, "batch of %lld tokens is too large", m);
+    *M = (int)m;
+    *G = (int)g;
+    *maxlen = ml;
+    return LAYA_OK;
+}
+
+int read_err(laya_ctx* c) {
+    const int e = *c->h_err;
+    if (e == 0) return LAYA_OK;
+    *c->h_err = 0;
+    cudaMemsetAsync(c->d_err, 0, 4, c->stream);
+    cudaStreamSynchronize(c->stream);
+    if (e & ERR_WAIT_TIMEOUT) return fail(c, LAYA_ERR_TIMEOUT, "a kernel gave up waiting (device error word %d)", e);
+    return fail(c, LAYA_ERR_ARG, "a kernel rejected an index (device error word %d)", e);
+}
+
+// Stage a host batch into the workspace; returns the device-side view.
+int stage_batch(laya_ctx* c, const laya_seq* seqs, uint32_t n, int M, int G, int maxlen, Batch* b) {
+    const int S = (int)n;
+    int rc = ensure_workspace(c, M, S, G);
+    if (rc) return rc;
+    uint8_t* h = static_cast<uint8_t*>(c->h_stage);
+    uint32_t* h_ids = reinterpret_cast<uint32_t*>(h);
+    int* h_cu = reinterpret_cast<int*>(h_ids + M);
+    uint32_t* h_qt = reinterpret_cast<uint32_t*>(h_cu + S + 1);
+    uint32_t* h_mk = h_qt + S;
+    int* h_cum = reinterpret_cast<int*>(h_mk + G);
+    int tok = 0, g = 0;
+    h_cu[0] = 0;
+    h_cum[0] = 0;
+    for (int s = 0; s < S; s++) {
+        memcpy(h_ids + tok, seqs[s].ids, seqs[s].len * 4);
+        if (seqs[s].n_markers) memcpy(h_mk + g, seqs[s].markers, seqs[s].n_markers * 4);
+        tok += seqs[s].len;
+        g += seqs[s].n_markers;
+        h_cu[s + 1] = tok;
+        h_cum[s + 1] = g;
+        h_qt[s] = seqs[s].qtype;
+    }
+    CK(cudaMemcpyAsync(c->d_ids, h_ids, (size_t)M * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_cu, h_cu, (size_t)(S + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_qt, h_qt, (size_t)S * 4, cudaMemcpyHostToDevice, c->stream));
+    if (G) CK(cudaMemcpyAsync(c->d_mk, h_mk, (size_t)G * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_cum, h_cum, (size_t)(S + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+    *b = Batch{c->d_ids, c->d_cu, c->d_mk, c->d_cum, c->d_qt, S, M, G, maxlen};
+    return LAYA_OK;
+}
+
+void rope_table(std::vector<float2>& t) {
+    // inv_freq (src/main.zig:2399-2401) and f32 cos/sin of inv*pos (2503-2506)
+    float inv[32];
+    for (int j = 0; j < 32; j++) inv[j] = 1.0f / powf(ROPE_THETA, (float)j / 32.0f);
+    t.resize((size_t)MAX_POS * 32);
+    for (int p = 0; p < MAX_POS; p++)
+        for (int j = 0; j < 32; j++) {
+            const float f = inv[j] * (float)p;
+            t[(size_t)p * 32 + j] = make_float2(cosf(f), sinf(f));
+        }
+}
+
+int create_impl(laya_ctx* c, const laya_tensor* t, int n) {
+    CK(cudaSetDevice(c->device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, c->device));
+    if (prop.major != 10)
+        return fail(c, LAYA_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", c->device,
+                    prop.major, prop.minor);
+    c->num_sms = prop.multiProcessorCount;
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CK(cudaMalloc(&c->d_err, 4));
+    c->allocs.push_back(c->d_err);
+    CK(cudaMemset(c->d_err, 0, 4));
+    CK(cudaMallocHost(&c->h_err, 4));
+    *c->h_err = 0;
+
+    // one device staging buffer, as large as the largest tensor given
+    size_t stage_bytes = 0;
+    for (int i = 0; i < n; i++) stage_bytes = std::max(stage_bytes, (size_t)t[i].numel * elem_size(t[i].dtype));
+    void* staging = nullptr;
+    CK(cudaMalloc(&staging, stage_bytes ? stage_bytes : 256));
+    int rc = 0;
+    char nm[160];
+    auto MAT = [&](const char* name, uint64_t rows, uint64_t cols, void** dst, int glu) {
+        if (!rc) rc = upload(c, t, n, name, rows, cols, true, glu, dst, staging);
+    };
+    auto VEC = [&](const char* name, uint64_t numel, float** dst) {
+        if (!rc) rc = upload(c, t, n, name, 1, numel, false, 0, reinterpret_cast<void**>(dst), staging);
+    };
+    MAT("encoder.embeddings.tok_embeddings.weight", VOCAB, D, &c->emb, 0);
+    VEC("encoder.embeddings.norm.weight", D, &c->emb_norm);
+    VEC("encoder.final_norm.weight", D, &c->final_norm);
+    VEC("type_emb.weight", 3 * D, &c->type_emb);
+    for (int l = 0; l < NL && !rc; l++) {
+        EncW& w = c->enc[l];
+        w.attn_norm = nullptr;
+        if (l > 0) {
+            snprintf(nm, sizeof nm, "encoder.layers.%d.attn_norm.weight", l);
+            VEC(nm, D, &w.attn_norm);
+        }
+        snprintf(nm, sizeof nm, "encoder.layers.%d.attn.Wqkv.weight", l);
+        MAT(nm, 3 * D, D, &w.wqkv, 0);
+        snprintf(nm, sizeof nm, "encoder.layers.%d.attn.Wo.weight", l);
+        MAT(nm, D, D, &w.wo, 0);
+        snprintf(nm, sizeof nm, "encoder.layers.%d.mlp.Wi.weight", l);
+        MAT(nm, 2 * INTER, D, &w.wi, 256);
+        snprintf(nm, sizeof nm, "encoder.layers.%d.mlp.Wo.weight", l);
+        MAT(nm, D, INTER, &w.wo2, 0);
+        snprintf(nm, sizeof nm, "encoder.layers.%d.mlp_norm.weight", l);
+        VEC(nm, D, &w.mlp_norm);
+        if (!rc) rc = weight_map(c, &w.m_qkv, w.wqkv, 3 * D, D);
+        if (!rc) rc = weight_map(c, &w.m_wo, w.wo, D, D);
+        if (!rc) rc = weight_map(c, &w.m_wi, w.wi, 2 * INTER, D);
+        if (!rc) rc = weight_map(c, &w.m_wo2, w.wo2, D, INTER);
+    }
+    for (int l = 0; l < HEAD_LAYERS && !rc; l++) {
+        HeadW& w = c->head[l];
+        auto N = [&](const char* s) {
+            snprintf(nm, sizeof nm, "head.layers.%d.%s", l, s);
+            return nm;
+        };
+        VEC(N("norm1.weight"), D, &w.n1w);
+        VEC(N("norm1.bias"), D, &w.n1b);
+        VEC(N("norm2.weight"), D, &w.n2w);
+        VEC(N("norm2.bias"), D, &w.n2b);
+        MAT(N("self_attn.in_proj_weight"), 3 * D, D, &w.in_w, 0);
+        VEC(N("self_attn.in_proj_bias"), 3 * D, &w.in_b);
+        MAT(N("self_attn.out_proj.weight"), D, D, &w.out_w, 0);
+        VEC(N("self_attn.out_proj.bias"), D, &w.out_b);
+        MAT(N("linear1.weight"), HEAD_FF, D, &w.l1_w, 0);
+        VEC(N("linear1.bias"), HEAD_FF, &w.l1_b);
+        MAT(N("linear2.weight"), D, HEAD_FF, &w.l2_w, 0);
+        VEC(N("linear2.bias"), D, &w.l2_b);
+        if (!rc) rc = weight_map(c, &w.m_in, w.in_w, 3 * D, D);
+        if (!rc) rc = weight_map(c, &w.m_out, w.out_w, D, D);
+        if (!rc) rc = weight_map(c, &w.m_l1, w.l1_w, HEAD_FF, D);
+        if (!rc) rc = weight_map(c, &w.m_l2, w.l2_w, D, HEAD_FF);
+    }
+    float *s0w, *s0b, *s1w, *s1b, *s3w, *s3b, *a0w, *a0b, *a2w, *a2b;
+    VEC("scorer.0.weight", D, &s0w);
+    VEC("scorer.0.bias", D, &s0b);
+    VEC("scorer.1.weight", (uint64_t)D * D, &s1w);
+    VEC("scorer.1.bias", D, &s1b);
+    VEC("scorer.3.weight", D, &s3w);
+    VEC("scorer.3.bias", 1, &s3b);
+    VEC("act_head.0.weight", 256 * (D + 4), &a0w);
+    VEC("act_head.0.bias", 256, &a0b);
+    VEC("act_head.2.weight", 2 * 256, &a2w);
+    VEC("act_head.2.bias", 2, &a2b);
+    cudaFree(staging);
+    if (rc) return rc;
+    c->tail = TailWeights{s0w, s0b, s1w, s1b, s3w, s3b, a0w, a0b, a2w, a2b};
+
+    std::vector<float2> rt;
+    rope_table(rt);
+    rc = dev_alloc(c, reinterpret_cast<void**>(&c->rope), rt.size() * sizeof(float2), c->allocs);
+    if (rc) return rc;
+    CK(cudaMemcpy(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    CK(gemm_prepare());
+    return LAYA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int laya_gpu_version(void) { return LAYA_GPU_ABI_VERSION; }
+
+int laya_gpu_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+const char* laya_gpu_last_error(const laya_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_error.c_str(); }
+
+void laya_gpu_destroy(laya_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    free_workspace(c);
+    for (void* p : c->allocs) cudaFree(p);
+    if (c->h_err) cudaFreeHost(c->h_err);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+int laya_gpu_create(int device, const laya_tensor* tensors, int n_tensors, int precision, laya_ctx** out) {
+    if (!out) return fail(nullptr, LAYA_ERR_ARG, "out is NULL");
+    *out = nullptr;
+    if (!tensors || n_tensors <= 0) return fail(nullptr, LAYA_ERR_ARG, "no tensors given");
+    if (precision != LAYA_PREC_BF16 && precision != LAYA_PREC_F16)
+        return fail(nullptr, LAYA_ERR_ARG, "precision %d (expected LAYA_PREC_BF16 or LAYA_PREC_F16)", precision);
+    const int ndev = laya_gpu_device_count();
+    if (device < 0 || device >= ndev)
+        return fail(nullptr, LAYA_ERR_NO_DEVICE, "device %d requested, %d visible", device, ndev);
+    laya_ctx* c = new laya_ctx();
+    c->device = device;
+    c->bf16 = precision == LAYA_PREC_BF16;
+    const int rc = create_impl(c, tensors, n_tensors);
+    if (rc) {
+        g_create_error = c->err;
+        laya_gpu_destroy(c);
+        return rc;
+    }
+    *out = c;
+    return LAYA_OK;
+}
+
+int laya_gpu_forward_batch(laya_ctx* c, const laya_seq* seqs, uint32_t n, float* logits, float* act, float* pooled,
+                           float* hidden) {
+    if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
+    if (!seqs || n == 0) return fail(c, LAYA_ERR_ARG, "empty batch");
+    if (!act) return fail(c, LAYA_ERR_ARG, "act is NULL");
+    CK(cudaSetDevice(c->device));
+    int M, G, maxlen;
+    int rc = check_seqs(c, seqs, n, &M, &G, &maxlen);
+    if (rc) return rc;
+    if (G && !logits) return fail(c, LAYA_ERR_ARG, "logits is NULL");
+    Batch b;
+    rc = stage_batch(c, seqs, n, M, G, maxlen, &b);
+    if (rc) return rc;
+    float* d_hidden = nullptr;
+    if (hidden) d_hidden = reinterpret_cast<float*>(c->qkv);  // free after the forward; M*D*4 <= M*3*D*2
+    Outs o{c->d_logits, c->d_act, pooled ? c->d_pooled : nullptr, d_hidden};
+    rc = launch_forward(c, b, o, c->stream);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
+    if (G) CK(cudaMemcpyAsync(logits, c->d_logits, (size_t)G * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(act, c->d_act, (size_t)n * 8, cudaMemcpyDeviceToHost, c->stream));
+    if (pooled) CK(cudaMemcpyAsync(pooled, c->d_pooled, (size_t)n * D * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (hidden) CK(cudaMemcpyAsync(hidden, d_hidden, (size_t)M * D * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return read_err(c);
+}
+
+int laya_gpu_forward(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers,
+                     uint32_t K, float* logits, float* act, float* pooled, float* hidden) {
+    if (!pooled) return fail(c, LAYA_ERR_ARG, "pooled is NULL");
+    laya_seq s{ids, L, markers, K, qtype};
+    return laya_gpu_forward_batch(c, &s, 1, logits, act, pooled, hidden);
+}
+
+int laya_gpu_forward_device(laya_ctx* c, const laya_batch* bt, float* logits, float* act, float* pooled,
+                            float* hidden, void* stream) {
+    if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
+    if (!bt || bt->n_seqs == 0 || bt->n_tokens == 0) return fail(c, LAYA_ERR_ARG, "empty batch");
+    if (bt->max_len == 0 || bt->max_len > LAYA_MAX_LEN)
+        return fail(c, LAYA_ERR_ARG, "max_len %u outside [1, %d]", bt->max_len, LAYA_MAX_LEN);
+    if (!bt->ids || !bt->cu_seqlens || !bt->cu_markers || !bt->qtypes || !act || (bt->n_markers && (!bt->markers || !logits)))
+        return fail(c, LAYA_ERR_ARG, "NULL input or output pointer");
+    CK(cudaSetDevice(c->device));
+    int rc = ensure_workspace(c, (int)bt->n_tokens, (int)bt->n_seqs, (int)bt->n_markers);
+    if (rc) return rc;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    Batch b{bt->ids, bt->cu_seqlens, bt->markers, bt->cu_markers, bt->qtypes, (int)bt->n_seqs, (int)bt->n_tokens,
+            (int)bt->n_markers, (int)bt->max_len};
+    Outs o{logits, act, pooled, hidden};
+    return launch_forward(c, b, o, s);
+}
+
+int laya_gpu_sync(laya_ctx* c) {
+    if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
+    CK(cudaSetDevice(c->device));
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost));
+    return read_err(c);
+}
+
+int laya_gpu_forward_trace(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers,
+                           uint32_t K, float* logits, float* act, float* trace) {
+    if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
+    if (!trace || !act) return fail(c, LAYA_ERR_ARG, "NULL output");
+    CK(cudaSetDevice(c->device));
+    laya_seq sq{ids, L, markers, K, qtype};
+    int M, G, maxlen;
+    int rc = check_seqs(c, &sq, 1, &M, &G, &maxlen);
+    if (rc) return rc;
+    if (G && !logits) return fail(c, LAYA_ERR_ARG, "logits is NULL");
+    Batch b;
+    rc = stage_batch(c, &sq, 1, M, G, maxlen, &b);
+    if (rc) return rc;
+    Outs o{c->d_logits, c->d_act, nullptr, nullptr};
+    const size_t LD = (size_t)L * D;
+    TraceHook hook{c, trace, LD};
+    cudaError_t e = run_forward(c, b, o, c->stream, hook);
+    if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
+    if (G) CK(cudaMemcpyAsync(logits, c->d_logits, (size_t)G * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(act, c->d_act, 8, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    // The GPU fuses the final norm with the type embedding; the "final" tag
+    // is recovered on the host as temb - type_emb[qtype].
+    std::vector<float> te(3 * D);
+    CK(cudaMemcpy(te.data(), c->type_emb, te.size() * 4, cudaMemcpyDeviceToHost));
+    float* fin = trace + 23 * LD;
+    const float* tmb = trace + 24 * LD;
+    for (size_t i = 0; i < LD; i++) fin[i] = tmb[i] - te[qtype * D + i % D];
+    return read_err(c);
+}
+
+int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, float* act, int iters, void* stream,
+                             float* stage_ms, int* stage_launches) {
+    if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
+    if (!bt || bt->n_seqs == 0 || bt->n_tokens == 0 || bt->max_len == 0 || bt->max_len > LAYA_MAX_LEN || iters <= 0 ||
+        !stage_ms || !act || (bt->n_markers && !logits))
+        return fail(c, LAYA_ERR_ARG, "profile: bad batch or NULL output");
+    CK(cudaSetDevice(c->device));
+    int rc = ensure_workspace(c, (int)bt->n_tokens, (int)bt->n_seqs, (int)bt->n_markers);
+    if (rc) return rc;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    Batch b{bt->ids, bt->cu_seqlens, bt->markers, bt->cu_markers, bt->qtypes, (int)bt->n_seqs, (int)bt->n_tokens,
+            (int)bt->n_markers, (int)bt->max_len};
+    Outs o{logits, act, nullptr, nullptr};
+    for (int i = 0; i < LAYA_N_STAGES; i++) stage_ms[i] = 0.f;
+    ProfileHook hook;
+    hook.s = s;
+    for (int it = 0; it < iters; it++) {
+        for (int i = 0; i < LAYA_N_STAGES; i++) hook.launches[i] = 0;
+        cudaError_t e = run_forward(c, b, o, s, hook);
+        if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile forward: %s", cudaGetErrorString(e));
+        CK(cudaStreamSynchronize(s));
+        hook.collect(stage_ms);
+    }
+    if (stage_launches)
+        for (int i = 0; i < LAYA_N_STAGES; i++) stage_launches[i] = hook.launches[i];
+    CK(cudaMemcpy(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost));
+    return read_err(c);
+}
+
+int laya_gpu_linear(const void* x, const void* w, const float* bias, float* out, int M, int N, int K, int elem_dtype,
+                    void* stream) {
+    laya_ctx* c = nullptr;
+    if (!x || !w || !out || M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 64)
+        return fail(c, LAYA_ERR_ARG, "linear: bad shape or NULL pointer (M=%d N=%d K=%d)", M, N, K);
+    if (elem_dtype != LAYA_DT_BF16 && elem_dtype != LAYA_DT_F16)
+        return fail(c, LAYA_ERR_DTYPE, "linear: elem_dtype %d", elem_dtype);
+    if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)out | (uintptr_t)bias) & 15)
+        return fail(c, LAYA_ERR_ARG, "linear: pointers must be 16-byte aligned");
+    const bool bf16 = elem_dtype == LAYA_DT_BF16;
+    const int bn = N % 256 == 0 ? 256 : 128;
+    int dev = 0, sms = 148;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CK(gemm_prepare());
+    static int* d_err[64] = {nullptr};
+    if (dev < 64 && !d_err[dev]) {
+        CK(cudaMalloc(&d_err[dev], 4));
+        CK(cudaMemset(d_err[dev], 0, 4));
+    }
+    CUtensorMap am, bm;
+    if (make_tmap_2d(&am, x, K, M, 128, bf16) != CUDA_SUCCESS || make_tmap_2d(&bm, w, K, N, bn, bf16) != CUDA_SUCCESS)
+        return fail(c, LAYA_ERR_CUDA, "linear: cuTensorMapEncodeTiled failed");
+    GemmArgs g{};
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.out_f32 = out;
+    g.ldo = N;
+    g.err = d_err[dev < 64 ? dev : 0];
+    CK(launch_gemm(EPI_F32, bn, bf16, am, bm, g, sms, static_cast<cudaStream_t>(stream)));
+    return LAYA_OK;
+}
+
+}  // extern "C"

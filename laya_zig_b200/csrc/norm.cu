@@ -1,0 +1,228 @@
+// norm.cu -- LayerNorm, embedding gather and the final-norm/type-embedding
+// step, one warp per 768-wide row with 16-byte loads and stores.
+//
+// LayerNorm is the reference's two-pass form (src/main.zig:83-95): mean,
+// then the mean of squared deviations, r = 1/sqrt(var + 1e-5), out =
+// (x - mean) * r * w (+ b). The sums run as warp reductions instead of one
+// sequential f32 chain.
+#include "kernels.cuh"
+
+namespace laya {
+namespace {
+
+// Lane `lane` owns elements [i*256 + lane*8, +8) for i = 0..2.
+struct Row {
+    float v[24];
+};
+
+__device__ __forceinline__ void load_f32_row(Row& r, const float* src, int lane) {
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const float4* p = reinterpret_cast<const float4*>(src + i * 256 + lane * 8);
+        const float4 a = p[0], b = p[1];
+        r.v[8 * i + 0] = a.x; r.v[8 * i + 1] = a.y; r.v[8 * i + 2] = a.z; r.v[8 * i + 3] = a.w;
+        r.v[8 * i + 4] = b.x; r.v[8 * i + 5] = b.y; r.v[8 * i + 6] = b.z; r.v[8 * i + 7] = b.w;
+    }
+}
+
+__device__ __forceinline__ void store_f32_row(float* dst, const Row& r, int lane) {
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        float4* p = reinterpret_cast<float4*>(dst + i * 256 + lane * 8);
+        p[0] = make_float4(r.v[8 * i + 0], r.v[8 * i + 1], r.v[8 * i + 2], r.v[8 * i + 3]);
+        p[1] = make_float4(r.v[8 * i + 4], r.v[8 * i + 5], r.v[8 * i + 6], r.v[8 * i + 7]);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f(T x);
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ void load16_row(Row& r, const T* src, int lane) {
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + i * 256 + lane * 8);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; j++) r.v[8 * i + j] = to_f<T>(e[j]);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pk(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pk<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pk<__half>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename T>
+__device__ __forceinline__ void store16_row(T* dst, const Row& r, int lane) {
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        uint4 u;
+        u.x = pk<T>(r.v[8 * i + 0], r.v[8 * i + 1]);
+        u.y = pk<T>(r.v[8 * i + 2], r.v[8 * i + 3]);
+        u.z = pk<T>(r.v[8 * i + 4], r.v[8 * i + 5]);
+        u.w = pk<T>(r.v[8 * i + 6], r.v[8 * i + 7]);
+        *reinterpret_cast<uint4*>(dst + i * 256 + lane * 8) = u;
+    }
+}
+
+// In-place LayerNorm of the row held across the warp.
+__device__ __forceinline__ void layer_norm(Row& r, const float* w, const float* b, int lane) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 24; i++) s += r.v[i];
+    const float mean = warp_sum(s) * (1.0f / D);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 24; i++) {
+        const float d = r.v[i] - mean;
+        q += d * d;
+    }
+    const float rs = 1.0f / sqrtf(warp_sum(q) * (1.0f / D) + LN_EPS);
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const float4* wp = reinterpret_cast<const float4*>(w + i * 256 + lane * 8);
+        const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float bb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (b) {
+            const float4* bp = reinterpret_cast<const float4*>(b + i * 256 + lane * 8);
+            const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+            bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
+            bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) r.v[8 * i + j] = (r.v[8 * i + j] - mean) * rs * ww[j] + bb[j];
+    }
+}
+
+__device__ __forceinline__ int find_seq(const int* cu, int n, int t) {
+    int lo = 0, hi = n;  // cu[lo] <= t < cu[hi]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (cu[mid] <= t) lo = mid;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// embedJob + normJob (src/main.zig:2543-2555): x = LN(E[id]); also writes the
+// 16-bit copy layer 0 multiplies (its attn_norm is the identity) and, per
+// token, its position in its sequence and the sequence index.
+template <typename T>
+__global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, int n_seqs, int M,
+                             const T* __restrict__ emb, const float* __restrict__ w, float* __restrict__ x,
+                             T* __restrict__ xn, int* __restrict__ pos, int* __restrict__ seq_of, int* err) {
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= M) return;
+    uint32_t id = ids[t];
+    if (id >= (uint32_t)VOCAB) {
+        if (lane == 0) atomicOr(err, ERR_BAD_INDEX);
+        id = 0;
+    }
+    if (lane == 0) {
+        const int s = find_seq(cu, n_seqs, t);
+        seq_of[t] = s;
+        pos[t] = t - cu[s];
+    }
+    Row r;
+    load16_row<T>(r, emb + (size_t)id * D, lane);
+    layer_norm(r, w, nullptr, lane);
+    store_f32_row(x + (size_t)t * D, r, lane);
+    store16_row<T>(xn + (size_t)t * D, r, lane);
+}
+
+// normIntoJob (src/main.zig:2596-2603): xn = LN(x), x untouched.
+template <typename T>
+__global__ void ln_kernel(const float* __restrict__ x, T* __restrict__ xn, const float* __restrict__ w,
+                          const float* __restrict__ b, int M) {
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= M) return;
+    Row r;
+    load_f32_row(r, x + (size_t)t * D, lane);
+    layer_norm(r, w, b, lane);
+    store16_row<T>(xn + (size_t)t * D, r, lane);
+}
+
+// final LN + typeEmbJob (src/main.zig:2708-2711) fused with the first head
+// layer's norm1 (2716): x = LN_final(x) + type_emb[qtype of the row's
+// sequence]; xn = LN(x; w1, b1).
+template <typename T>
+__global__ void final_kernel(float* __restrict__ x, T* __restrict__ xn, const float* __restrict__ wf,
+                             const float* __restrict__ type_emb, const uint32_t* __restrict__ qtypes,
+                             const int* __restrict__ seq_of, const float* __restrict__ w1,
+                             const float* __restrict__ b1, int M) {
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= M) return;
+    Row r;
+    load_f32_row(r, x + (size_t)t * D, lane);
+    layer_norm(r, wf, nullptr, lane);
+    const uint32_t qt = qtypes[seq_of[t]];
+    Row te;
+    load_f32_row(te, type_emb + (size_t)(qt < 3 ? qt : 0) * D, lane);
+#pragma unroll
+    for (int i = 0; i < 24; i++) r.v[i] += te.v[i];
+    store_f32_row(x + (size_t)t * D, r, lane);
+    layer_norm(r, w1, b1, lane);
+    store16_row<T>(xn + (size_t)t * D, r, lane);
+}
+
+constexpr int ROWS_PER_BLOCK = 8;  // 256 threads
+
+}  // namespace
+
+cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_seqs, int M, const void* emb,
+                         const float* w, float* x, void* xn, int* pos, int* seq_of, int* err, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
+    if (bf16)
+        embed_kernel<__nv_bfloat16><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(
+            ids, cu, n_seqs, M, static_cast<const __nv_bfloat16*>(emb), w, x, static_cast<__nv_bfloat16*>(xn), pos,
+            seq_of, err);
+    else
+        embed_kernel<__half><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(ids, cu, n_seqs, M,
+                                                                   static_cast<const __half*>(emb), w, x,
+                                                                   static_cast<__half*>(xn), pos, seq_of, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
+    if (bf16)
+        ln_kernel<__nv_bfloat16><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(x, static_cast<__nv_bfloat16*>(xn), w, b, M);
+    else
+        ln_kernel<__half><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(x, static_cast<__half*>(xn), w, b, M);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const float* type_emb,
+                         const uint32_t* qtypes, const int* seq_of, const float* w1, const float* b1, int M,
+                         cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
+    if (bf16)
+        final_kernel<__nv_bfloat16><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(
+            x, static_cast<__nv_bfloat16*>(xn), wf, type_emb, qtypes, seq_of, w1, b1, M);
+    else
+        final_kernel<__half><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(x, static_cast<__half*>(xn), wf, type_emb,
+                                                                   qtypes, seq_of, w1, b1, M);
+    return cudaGetLastError();
+}
+
+}  // namespace laya

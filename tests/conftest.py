@@ -1,0 +1,51 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) and the built CUDA library")
+
+
+@pytest.fixture(scope="session")
+def weights():
+    from laya_zig_b200 import synth
+    return synth.make_weights(0)
+
+
+@pytest.fixture(scope="session")
+def oracle_model(weights):
+    from oracle import oracle
+    return oracle.model_from_bf16(weights)
+
+
+@pytest.fixture(scope="session")
+def gpu_model(weights):
+    from laya_zig_b200 import gpu
+    m = gpu.LayaGPU.from_bf16(weights, device=0)
+    yield m
+    m.close()
+
+
+def golden_cases():
+    import json
+    out = {}
+    for f in sorted(os.listdir(GOLDEN)):
+        if f.endswith(".json"):
+            with open(os.path.join(GOLDEN, f)) as fh:
+                out[f[:-5]] = json.load(fh)
+    return out
+
+
+def row_rel(got: np.ndarray, ref: np.ndarray) -> float:
+    """max over rows of max_j |g - r| / max_j |r| (the hidden-state metric)."""
+    got = np.atleast_2d(got).astype(np.float64)
+    ref = np.atleast_2d(ref).astype(np.float64)
+    return float((np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)).max())

@@ -1,0 +1,151 @@
+"""The CUDA forward pass against the oracle, through the C ABI.
+
+Tolerances (the path's stated bar):
+  * token ids: bit-exact (the same host arrays feed both sides);
+  * argmax option: identical;
+  * option probabilities: |dp| <= 1e-3;
+  * act/escalate probabilities: |dp| <= 1e-3;
+  * final hidden states: max over rows of max_j|g - r| / max_j|r| <= 2e-2.
+"""
+import numpy as np
+import pytest
+
+from conftest import golden_cases, row_rel
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN_TOL = 2e-2
+PROB_TOL = 1e-3
+
+
+def _probs(logits):
+    from laya_zig_b200.gpu import option_probs
+    return option_probs(logits, 0)
+
+
+def _compare(g, r, label=""):
+    """g: gpu Forward, r: oracle dict. Returns a dict of the measured errors."""
+    err = {}
+    if "hidden" in r and g.hidden is not None:
+        err["hidden"] = row_rel(g.hidden, r["hidden"])
+    if len(r["logits"]):
+        pg, pr = _probs(g.logits), _probs(r["logits"])
+        err["probs"] = float(np.abs(pg - pr).max())
+        err["logits"] = float(np.abs(g.logits - r["logits"]).max())
+        assert int(np.argmax(pg)) == int(np.argmax(pr)), (label, pg, pr)
+    err["act"] = float(np.abs(g.act - r["act"]).max())
+    err["pooled"] = row_rel(g.pooled, r["pooled"])
+    assert err.get("hidden", 0) <= HIDDEN_TOL, (label, err)
+    assert err.get("probs", 0) <= PROB_TOL, (label, err)
+    assert err["act"] <= PROB_TOL, (label, err)
+    assert err["pooled"] <= HIDDEN_TOL, (label, err)
+    return err
+
+
+def test_parity_c1(gpu_model, oracle_model):
+    from laya_zig_b200 import synth
+    d = synth.parity_decision(1)
+    g = gpu_model.forward(d.ids, d.qtype, d.markers, want_hidden=True)
+    r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+    err = _compare(g, r, "c1")
+    print("c1 errors", err)
+
+
+def test_trace_per_layer(gpu_model, oracle_model):
+    """--dumpstats analogue: the hidden state after every stage stays within tolerance."""
+    from laya_zig_b200 import synth
+    from laya_zig_b200.gpu import TRACE_TAGS
+    d = synth.parity_decision(1)
+    _, _, trace = gpu_model.forward_trace(d.ids, d.qtype, d.markers)
+    r = oracle_model.forward(d.ids, d.markers, d.qtype, want_trace=True)
+    errs = {t: row_rel(trace[i], r["trace"][i]) for i, t in enumerate(TRACE_TAGS)}
+    print("per-stage hidden error", {k: "%.2e" % v for k, v in errs.items()})
+    assert errs["emb"] < 1e-5
+    assert max(errs.values()) <= HIDDEN_TOL, errs
+
+
+@pytest.mark.parametrize("name", sorted(golden_cases()))
+def test_gpu_matches_refcheck_golden(name, gpu_model):
+    """Against the reference's own checker (tools/refcheck.py), directly."""
+    g = golden_cases()[name]
+    out = gpu_model.forward(np.array(g["ids"]), g["qtype"], np.array(g["markers"]), want_hidden=True)
+    for k, row in g["hidden_rows"].items():
+        assert row_rel(out.hidden[int(k)], np.array(row)) <= HIDDEN_TOL
+    if g["logits"]:
+        assert np.abs(_probs(out.logits) - np.array(g["probs"])).max() <= PROB_TOL
+        assert int(np.argmax(out.logits)) == int(np.argmax(g["logits"]))
+    assert np.abs(out.act - np.array(g["act"])).max() <= PROB_TOL
+
+
+def test_snake_batch_parity(gpu_model, oracle_model):
+    """Batch 64 x 175-180 tokens, 8 markers each, one packed pass vs the oracle per sequence."""
+    from laya_zig_b200 import synth
+    batch = synth.snake_batch(64)
+    outs = gpu_model.forward_batch(batch, want_pooled=True, want_hidden=True)
+    worst = {}
+    for i, (d, g) in enumerate(zip(batch, outs)):
+        r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+        e = _compare(g, r, "seq %d" % i)
+        for k, v in e.items():
+            worst[k] = max(worst.get(k, 0.0), v)
+    print("c3 worst errors", worst)
+
+
+def test_batch_equals_single(gpu_model):
+    """Packing never mixes sequences: a sequence's results do not depend on its batch."""
+    from laya_zig_b200 import synth
+    batch = synth.snake_batch(5, seed=9)
+    outs = gpu_model.forward_batch(batch, want_pooled=True)
+    for d, b in zip(batch, outs):
+        s = gpu_model.forward(d.ids, d.qtype, d.markers)
+        np.testing.assert_array_equal(s.logits, b.logits)
+        np.testing.assert_array_equal(s.act, b.act)
+        np.testing.assert_array_equal(s.pooled, b.pooled)
+
+
+def test_ragged_and_edge_sequences(gpu_model, oracle_model):
+    """Lengths around the tile and window edges, one token, no markers, every qtype."""
+    from laya_zig_b200 import synth
+    rng = np.random.Generator(np.random.PCG64(21))
+    cases = []
+    for L, K, qt in [(1, 1, 0), (1, 0, 1), (2, 2, 2), (63, 3, 0), (64, 1, 1), (65, 4, 2), (127, 2, 0), (128, 5, 1),
+                     (129, 6, 2), (130, 2, 0), (200, 0, 1), (257, 9, 2)]:
+        mk = sorted(rng.choice(L, size=K, replace=False).tolist()) if K else []
+        cases.append(synth._decision(rng, L, mk, qt))
+    outs = gpu_model.forward_batch(cases, want_pooled=True, want_hidden=True)
+    for d, g in zip(cases, outs):
+        r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+        _compare(g, r, "L=%d K=%d" % (len(d.ids), len(d.markers)))
+
+
+def test_input_errors(gpu_model):
+    from laya_zig_b200 import gpu
+    ok_ids = np.array([2, 7, 4, 1], dtype=np.uint32)
+    with pytest.raises(gpu.LayaError, match="vocab"):
+        gpu_model.forward(np.array([2, 256000, 1]), 0, [1])
+    with pytest.raises(gpu.LayaError, match="marker"):
+        gpu_model.forward(ok_ids, 0, [4])
+    with pytest.raises(gpu.LayaError, match="qtype"):
+        gpu_model.forward(ok_ids, 3, [2])
+    with pytest.raises(gpu.LayaError, match="length"):
+        gpu_model.forward(np.array([], dtype=np.uint32), 0, [])
+    # the context stays usable after rejected calls
+    out = gpu_model.forward(ok_ids, 0, [2])
+    assert np.isfinite(out.logits).all() and abs(out.act.sum() - 1) < 1e-5
+
+
+def test_create_errors(weights):
+    from laya_zig_b200 import gpu
+    w = {k: ("BF16", v) for k, v in weights.items()}
+    missing = dict(w)
+    del missing["head.layers.1.linear2.bias"]
+    with pytest.raises(gpu.MissingTensor, match="missing tensor: head.layers.1.linear2.bias"):
+        gpu.LayaGPU(missing)
+    bad_dtype = dict(w)
+    bad_dtype["scorer.1.weight"] = ("I8", weights["scorer.1.weight"])
+    with pytest.raises(gpu.UnsupportedDtype):
+        gpu.LayaGPU(bad_dtype)
+    bad_shape = dict(w)
+    bad_shape["encoder.layers.0.attn.Wo.weight"] = ("BF16", weights["encoder.layers.0.attn.Wo.weight"][:100])
+    with pytest.raises(gpu.LayaError, match="elements"):
+        gpu.LayaGPU(bad_shape)
