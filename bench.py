@@ -216,7 +216,9 @@ def main():
     logits = torch.zeros(G, dtype=torch.float32, device="cuda")
     act = torch.zeros((S, 2), dtype=torch.float32, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()          # every launch, flush and event of the timed loop goes here
+    torch.cuda.set_stream(stream)
     sp = stream.cuda_stream
 
     for _ in range(max(3, args.warmup)):

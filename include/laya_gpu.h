@@ -130,9 +130,10 @@ LAYA_API int laya_gpu_forward_batch(laya_ctx* ctx, const laya_seq* seqs, uint32_
                            float* pooled, float* hidden);
 
 /* Same pass over a batch already in device memory; outputs are device
- * pointers (pooled, hidden nullable). Asynchronous on `stream` (a
- * cudaStream_t; NULL = the context's stream); call laya_gpu_sync to wait
- * and to collect device-side errors. Inputs are not validated on the host:
+ * pointers (pooled, hidden nullable). Asynchronous on `stream`, a
+ * cudaStream_t of the context's device (NULL = the legacy default stream,
+ * as everywhere in CUDA); call laya_gpu_sync to wait and to collect
+ * device-side errors. Inputs are not validated on the host:
  * bad ids or markers are clamped and reported by laya_gpu_sync. */
 LAYA_API int laya_gpu_forward_device(laya_ctx* ctx, const laya_batch* batch, float* logits, float* act, float* pooled,
                             float* hidden, void* stream);
@@ -145,6 +146,17 @@ LAYA_API int laya_gpu_sync(laya_ctx* ctx);
  * l0..l21, final, temb, h0, h1. */
 LAYA_API int laya_gpu_forward_trace(laya_ctx* ctx, const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers,
                            uint32_t K, float* logits, float* act, float* trace);
+
+/* Finer than --dumpstats: every intermediate of encoder layer `layer`
+ * (0..21) for one sequence, as the GPU holds it. 16-bit buffers are raw
+ * element bits of the context's precision. xn_attn[L][768] (attn_norm
+ * output; layer 0: the embedding output), qkv[L][2304] (after RoPE),
+ * ctx[L][768] (attention output), x_mid[L][768] f32 (after the attention
+ * residual), xn_mlp[L][768] (mlp_norm output), glu[L][1152] (gelu(gate) *
+ * up). Any output may be NULL. */
+LAYA_API int laya_gpu_forward_dump(laya_ctx* ctx, const uint32_t* ids, uint32_t L, uint32_t qtype,
+                                   const uint32_t* markers, uint32_t K, int layer, uint16_t* xn_attn, uint16_t* qkv,
+                                   uint16_t* ctx_out, float* x_mid, uint16_t* xn_mlp, uint16_t* glu);
 
 /* Stages of the forward, as the reference's --profile buckets them
  * (src/main.zig:132-198): one entry per kernel family. */
@@ -162,8 +174,8 @@ typedef enum {
 } laya_stage;
 
 /* --profile: run `iters` forwards of a device batch eagerly (no graph) with
- * a CUDA event pair around every kernel on `stream` (NULL = the context's
- * stream). stage_ms[LAYA_N_STAGES] receives the summed kernel time per
+ * a CUDA event pair around every kernel on `stream` (a cudaStream_t, NULL =
+ * the legacy default stream). stage_ms[LAYA_N_STAGES] receives the summed kernel time per
  * stage over all iterations, stage_launches[LAYA_N_STAGES] the launches per
  * forward. Synchronous. */
 LAYA_API int laya_gpu_forward_profile(laya_ctx* ctx, const laya_batch* batch, float* logits, float* act, int iters,

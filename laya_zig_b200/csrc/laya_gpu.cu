@@ -159,7 +159,9 @@ int upload(laya_ctx* c, const laya_tensor* t, int n, const char* name, uint64_t 
     if (rc) return rc;
     rc = dev_alloc(c, dst, rows * cols * (matrix ? 2 : 4), c->allocs);
     if (rc) return rc;
-    CK(cudaMemcpy(staging, e->data, rows * cols * elem_size(e->dtype), cudaMemcpyHostToDevice));
+    // On the context's stream: a cudaMemcpy from pageable memory may return
+    // before its DMA lands, and c->stream does not wait on the legacy stream.
+    CK(cudaMemcpyAsync(staging, e->data, rows * cols * elem_size(e->dtype), cudaMemcpyHostToDevice, c->stream));
     if (matrix)
         CK(launch_convert16(*dst, c->bf16, staging, e->dtype, rows, cols, glu_tile, c->stream));
     else
@@ -185,7 +187,7 @@ void free_workspace(laya_ctx* c) {
 int ensure_workspace(laya_ctx* c, int M, int S, int G) {
     if (M <= c->capM && S <= c->capS && G <= c->capG) return LAYA_OK;
     const int nM = std::max(M, c->capM), nS = std::max(S, c->capS), nG = std::max(std::max(G, c->capG), 1);
-    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaDeviceSynchronize());  // device-path work may be pending on a caller's stream
     free_workspace(c);
     const size_t e16 = 2;
     int rc = 0;
@@ -336,6 +338,40 @@ struct TraceHook {
     void tap(int tag) { cudaMemcpyAsync(trace + (size_t)tag * LD, c->x, LD * 4, cudaMemcpyDeviceToHost, c->stream); }
 };
 
+// Copies every intermediate of one encoder layer to the host.
+struct DumpHook {
+    laya_ctx* c;
+    int target, M;
+    uint16_t *xn_attn, *qkv, *ctx, *xn_mlp, *glu;
+    float* x_mid;
+    int cur = -1, norms = 0;
+    void get(void* dst, const void* src, size_t bytes) {
+        if (dst) cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->stream);
+    }
+    void begin(int) {}
+    void extra(int, int) {}
+    void end(int st) {
+        if (cur != target) return;
+        const size_t M16 = (size_t)M * 2;
+        switch (st) {
+            case LAYA_STAGE_NORM:
+                if (norms++ == 0 && target > 0) get(xn_attn, c->xn, M16 * D);
+                else get(xn_mlp, c->xn, M16 * D);
+                break;
+            case LAYA_STAGE_GEMM_QKV: get(qkv, c->qkv, M16 * 3 * D); break;
+            case LAYA_STAGE_ATTN: get(ctx, c->ctxb, M16 * D); break;
+            case LAYA_STAGE_GEMM_OUT: get(x_mid, c->x, (size_t)M * D * 4); break;
+            case LAYA_STAGE_GEMM_UP: get(glu, c->mlp, M16 * INTER); break;
+            default: break;
+        }
+    }
+    void tap(int tag) {
+        cur = tag;  // tag 0 follows the embedding, tag 1 + l follows layer l
+        norms = 0;
+        if (tag == 0 && target == 0) get(xn_attn, c->xn, (size_t)M * 2 * D);
+    }
+};
+
 // An event pair around every launch; per-stage times summed after a sync.
 struct ProfileHook {
     cudaStream_t s;
@@ -375,7 +411,8 @@ struct ProfileHook {
     }
 };
 
-// Run (capturing a graph on first use of this shape) on stream s.
+// Run on stream s (any stream, the legacy default one included), capturing
+// a graph on the context's own stream on first use of this shape.
 int launch_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t s) {
     GraphKey k{b.M, b.S, b.G, b.maxlen, b.ids, b.cu, b.mk, b.cum, b.qt, o.logits, o.act, o.pooled, o.hidden};
     auto it = c->graphs.find(k);
@@ -385,10 +422,10 @@ int launch_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t s) {
             c->graphs.clear();
         }
         cudaGraph_t graph;
-        CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
         NoHook hook;
-        cudaError_t e = run_forward(c, b, o, s, hook);
-        cudaError_t e2 = cudaStreamEndCapture(s, &graph);
+        cudaError_t e = run_forward(c, b, o, c->stream, hook);
+        cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
         if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "launch during capture: %s", cudaGetErrorString(e));
         if (e2 != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(e2));
         cudaGraphExec_t exec;
@@ -495,7 +532,7 @@ int create_impl(laya_ctx* c, const laya_tensor* t, int n) {
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     CK(cudaMalloc(&c->d_err, 4));
     c->allocs.push_back(c->d_err);
-    CK(cudaMemset(c->d_err, 0, 4));
+    CK(cudaMemsetAsync(c->d_err, 0, 4, c->stream));
     CK(cudaMallocHost(&c->h_err, 4));
     *c->h_err = 0;
 
@@ -580,7 +617,8 @@ int create_impl(laya_ctx* c, const laya_tensor* t, int n) {
     rope_table(rt);
     rc = dev_alloc(c, reinterpret_cast<void**>(&c->rope), rt.size() * sizeof(float2), c->allocs);
     if (rc) return rc;
-    CK(cudaMemcpy(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
     CK(gemm_prepare());
     return LAYA_OK;
 }
@@ -678,7 +716,7 @@ int laya_gpu_forward_device(laya_ctx* c, const laya_batch* bt, float* logits, fl
     CK(cudaSetDevice(c->device));
     int rc = ensure_workspace(c, (int)bt->n_tokens, (int)bt->n_seqs, (int)bt->n_markers);
     if (rc) return rc;
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);  // 0 = the legacy default stream
     Batch b{bt->ids, bt->cu_seqlens, bt->markers, bt->cu_markers, bt->qtypes, (int)bt->n_seqs, (int)bt->n_tokens,
             (int)bt->n_markers, (int)bt->max_len};
     Outs o{logits, act, pooled, hidden};
@@ -725,6 +763,28 @@ int laya_gpu_forward_trace(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_
     return read_err(c);
 }
 
+int laya_gpu_forward_dump(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers,
+                          uint32_t K, int layer, uint16_t* xn_attn, uint16_t* qkv, uint16_t* ctx_out, float* x_mid,
+                          uint16_t* xn_mlp, uint16_t* glu) {
+    if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
+    if (layer < 0 || layer >= NL) return fail(c, LAYA_ERR_ARG, "layer %d outside [0, %d)", layer, NL);
+    CK(cudaSetDevice(c->device));
+    laya_seq sq{ids, L, markers, K, qtype};
+    int M, G, maxlen;
+    int rc = check_seqs(c, &sq, 1, &M, &G, &maxlen);
+    if (rc) return rc;
+    Batch b;
+    rc = stage_batch(c, &sq, 1, M, G, maxlen, &b);
+    if (rc) return rc;
+    Outs o{c->d_logits, c->d_act, nullptr, nullptr};
+    DumpHook hook{c, layer, M, xn_attn, qkv, ctx_out, xn_mlp, glu, x_mid};
+    cudaError_t e = run_forward(c, b, o, c->stream, hook);
+    if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return read_err(c);
+}
+
 int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, float* act, int iters, void* stream,
                              float* stage_ms, int* stage_launches) {
     if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
@@ -734,7 +794,7 @@ int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, f
     CK(cudaSetDevice(c->device));
     int rc = ensure_workspace(c, (int)bt->n_tokens, (int)bt->n_seqs, (int)bt->n_markers);
     if (rc) return rc;
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);  // 0 = the legacy default stream
     Batch b{bt->ids, bt->cu_seqlens, bt->markers, bt->cu_markers, bt->qtypes, (int)bt->n_seqs, (int)bt->n_tokens,
             (int)bt->n_markers, (int)bt->max_len};
     Outs o{logits, act, nullptr, nullptr};
@@ -773,6 +833,7 @@ int laya_gpu_linear(const void* x, const void* w, const float* bias, float* out,
     if (dev < 64 && !d_err[dev]) {
         CK(cudaMalloc(&d_err[dev], 4));
         CK(cudaMemset(d_err[dev], 0, 4));
+        CK(cudaDeviceSynchronize());  // the launch below may be on a stream that does not wait on this one
     }
     CUtensorMap am, bm;
     if (make_tmap_2d(&am, x, K, M, 128, bf16) != CUDA_SUCCESS || make_tmap_2d(&bm, w, K, N, bn, bf16) != CUDA_SUCCESS)

