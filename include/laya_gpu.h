@@ -181,6 +181,28 @@ typedef enum {
 LAYA_API int laya_gpu_forward_profile(laya_ctx* ctx, const laya_batch* batch, float* logits, float* act, int iters,
                                       void* stream, float* stage_ms, int* stage_launches);
 
+/* The decision tail alone (option scorer + act/escalate head) over final
+ * hidden states the caller already holds in device memory, allocating
+ * nothing. No counterpart in the reference: it is for callers that cannot
+ * let a library call cudaMalloc at decision time (a process that gives all
+ * device memory to its own caching allocator, or a serving loop with a fixed
+ * memory budget), which the other entry points may do when a batch outgrows
+ * their workspace. Its scratch is a static device array sized for
+ * LAYA_NOALLOC_MAX_MARKERS markers (6.4 MB, held by every GPU that loads
+ * the library until exit); larger calls are rejected with LAYA_ERR_ARG.
+ * hidden[n_tokens][768] f32, cu_seqlens/cu_markers[n_seqs + 1],
+ * markers[n_markers]; outputs logits[n_markers], act[2 * n_seqs],
+ * pooled[n_seqs][768], all device pointers. Asynchronous on `stream` (NULL
+ * = the legacy default stream); laya_gpu_sync reports device-side errors.
+ * The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress, which may load the module): make it before any
+ * stream capture. Calls share the array: calls that overlap on the GPU race. */
+#define LAYA_NOALLOC_MAX_MARKERS 2048
+LAYA_API int laya_gpu_decision_tail_noalloc(laya_ctx* ctx, const float* hidden, const int32_t* cu_seqlens,
+                                            const uint32_t* markers, const int32_t* cu_markers, uint32_t n_seqs,
+                                            uint32_t n_markers, float* logits, float* act, float* pooled,
+                                            void* stream);
+
 /* One projection, device pointers: out[M][N] (f32) = x[M][K] . w[N][K]^T
  * (+ bias[N]); x and w 16-bit of `elem_dtype` (LAYA_DT_BF16 or LAYA_DT_F16).
  * N a multiple of 128, K a multiple of 64; device pointers 16-byte aligned.

@@ -625,6 +625,18 @@ int create_impl(laya_ctx* c, const laya_tensor* t, int n) {
 
 }  // namespace
 
+// For tail_noalloc.cu: the tail weights, device and error word of a context,
+// and a way to record a failure on it.
+int laya_ctx_tail_view(laya_ctx* c, TailWeights* w, int* device, int** d_err) {
+    if (!c) return LAYA_ERR_ARG;
+    *w = c->tail;
+    *device = c->device;
+    *d_err = c->d_err;
+    return LAYA_OK;
+}
+
+int laya_ctx_fail(laya_ctx* c, int code, const char* msg) { return fail(c, code, "%s", msg); }
+
 extern "C" {
 
 int laya_gpu_version(void) { return LAYA_GPU_ABI_VERSION; }

@@ -102,6 +102,8 @@ def _load():
     L.laya_gpu_forward_profile.restype = I
     L.laya_gpu_forward_dump.argtypes = [P, P, U, U, P, U, I, P, P, P, P, P, P]
     L.laya_gpu_forward_dump.restype = I
+    L.laya_gpu_decision_tail_noalloc.argtypes = [P, P, P, P, P, U, U, P, P, P, P]
+    L.laya_gpu_decision_tail_noalloc.restype = I
     return L
 
 
@@ -252,6 +254,17 @@ class LayaGPU:
 
     def sync(self) -> None:
         self._check(lib.laya_gpu_sync(self._h))
+
+    def decision_tail_noalloc(self, hidden_ptr: int, batch: "DeviceBatch", logits_ptr: int, act_ptr: int,
+                              pooled_ptr: int, stream: int = 0) -> None:
+        """Scorer + act head over device-resident final hidden states, for
+        callers that cannot have the library allocate device memory: the
+        scratch is a static device array (at most 2048 markers per call).
+        Asynchronous on `stream`; calls that overlap on the GPU race."""
+        b = batch.c
+        self._check(lib.laya_gpu_decision_tail_noalloc(self._h, hidden_ptr, b.cu_seqlens, b.markers, b.cu_markers,
+                                                       b.n_seqs, b.n_markers, logits_ptr or None, act_ptr,
+                                                       pooled_ptr, stream or None))
 
     def profile(self, batch: "DeviceBatch", logits_ptr: int, act_ptr: int, iters: int = 1, stream: int = 0):
         """--profile (src/main.zig:132-198): ({stage: summed kernel ms}, {stage: launches per forward})
