@@ -1,14 +1,17 @@
 // gemm.cu -- persistent tcgen05 GEMM for the projection layers.
 //
-// One CTA per SM, 192 threads, warp-specialised:
+// One CTA per SM, 320 threads, warp-specialised:
 //   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per
 //               k-block into a STAGES-deep shared-memory ring (128B swizzle).
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
 //               K=16) into a double-buffered f32 accumulator in TMEM and
 //               commits to mbarriers (ring slot free / accumulator full).
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp owns the
-//               32 TMEM lanes = tile rows its warp id allows), the fused
-//               elementwise op of the layer, 16-byte global stores.
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (each warp may only
+//               read the 32 lanes = tile rows its warp id selects), one per
+//               half of the tile's columns: tcgen05.ld of the accumulator,
+//               the fused elementwise op, a swizzled 32 x 128-byte tile in
+//               shared memory, and a TMA store of it (the residual stream: a
+//               TMA reduce-add, so the f32 stream is never read by the SM).
 // The accumulator is double-buffered, so the epilogue of tile i overlaps the
 // MMAs of tile i+1. Every wait is bounded (common.cuh); a CTA that gives up
 // records the error, drains its own TMA loads and MMAs, frees TMEM and exits.
@@ -27,7 +30,9 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+constexpr int STAGING_BYTES = 32 * 128;  // one 32-row x 128-byte output tile per epilogue warp
 
 template <int BN>
 struct Cfg {
@@ -35,8 +40,9 @@ struct Cfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int RING = STAGES * STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // two accumulators of BN f32 columns
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int SMEM = RING + EPI_WARPS * STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 template <typename T>
@@ -65,20 +71,6 @@ __device__ __forceinline__ void load_cols(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-template <typename T>
-__device__ __forceinline__ void store16x32(T* dst, const float (&v)[32]) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-        uint4 u;
-        u.x = Pack<T>::two(v[8 * q + 0], v[8 * q + 1]);
-        u.y = Pack<T>::two(v[8 * q + 2], v[8 * q + 3]);
-        u.z = Pack<T>::two(v[8 * q + 4], v[8 * q + 5]);
-        u.w = Pack<T>::two(v[8 * q + 6], v[8 * q + 7]);
-        d[q] = u;
-    }
-}
-
 __device__ __forceinline__ void add_bias(float (&v)[32], const float* bias, int col) {
     if (bias) {
         const float4* b = reinterpret_cast<const float4*>(bias + col);
@@ -93,92 +85,156 @@ __device__ __forceinline__ void add_bias(float (&v)[32], const float* bias, int 
     }
 }
 
+// Row `lane` of a 32 x 128-byte staging tile, 16-byte chunk `j`, in the
+// 128-byte swizzle the output tensor map expects (chunk j of row r lands at
+// chunk j ^ (r % 8)); the tile base is 1024-byte aligned.
+__device__ __forceinline__ uint4* stage_chunk(uint8_t* tile, int lane, int j) {
+    return reinterpret_cast<uint4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4));
+}
+
+// 32 values -> 64 bytes of 16-bit elements at chunks [c0, c0 + 4).
+template <typename T>
+__device__ __forceinline__ void stage16(uint8_t* tile, int lane, int c0, const float (&v)[32]) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        uint4 u;
+        u.x = Pack<T>::two(v[8 * q + 0], v[8 * q + 1]);
+        u.y = Pack<T>::two(v[8 * q + 2], v[8 * q + 3]);
+        u.z = Pack<T>::two(v[8 * q + 4], v[8 * q + 5]);
+        u.w = Pack<T>::two(v[8 * q + 6], v[8 * q + 7]);
+        *stage_chunk(tile, lane, c0 + q) = u;
+    }
+}
+
+// 32 f32 values -> the whole 128-byte row.
+__device__ __forceinline__ void stage32(uint8_t* tile, int lane, const float (&v)[32]) {
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+        *stage_chunk(tile, lane, q) =
+            make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
+                       __float_as_uint(v[4 * q + 3]));
+}
+
+// Hand the staged tile to the TMA unit: make the generic-proxy writes
+// visible to the async proxy, then one lane issues the store.
+template <bool REDUCE>
+__device__ __forceinline__ void flush_stage(const CUtensorMap* map, uint8_t* tile, int lane, int col, int row) {
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+        if (REDUCE) tma_reduce_add_2d(map, tile, col, row);
+        else tma_store_2d(map, tile, col, row);
+        bulk_commit();
+    }
+}
+
+// Before rewriting the staging tile: its previous store has read it.
+__device__ __forceinline__ void reuse_stage(int lane) {
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+}
+
 template <int BN, int EPI, typename T>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tacc, int row, int n_blk) {
-    const bool live = row < a.M;
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* out_map, uint8_t* tile,
+                                              uint32_t tacc, int half, int lane, int m0q, int n_blk) {
+    constexpr int HALF = BN / 2;  // accumulator columns this warp owns
     if constexpr (EPI == EPI_GLU) {
-        // columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows
-        constexpr int HALF = BN / 2;
+        // tile columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows;
+        // this warp produces output columns [half*BN/4, (half+1)*BN/4) of the tile
+        constexpr int OUT = BN / 4;
+        static_assert(OUT == 64 || OUT == 32, "GLU tile");
+#pragma unroll 1
+        for (int c = 0; c < OUT; c += 32) {
+            float g[32], u[32];
+            load_cols(tacc + half * OUT + c, g);
+            load_cols(tacc + HALF + half * OUT + c, u);
+#pragma unroll
+            for (int i = 0; i < 32; i++) g[i] = gelu_as(g[i]) * u[i];
+            if (c == 0) reuse_stage(lane);
+            stage16<T>(tile, lane, (c / 32) * 4, g);
+        }
+        flush_stage<false>(out_map, tile, lane, n_blk * HALF + half * OUT, m0q);
+    } else if constexpr (EPI == EPI_QKV) {
+        const int col0 = n_blk * BN + half * HALF;
+        const bool rope = col0 < a.rope_cols;
+        float4 cs[16];  // (cos, sin) of this row's position for the 32 frequencies, loaded once per tile
+        if (rope) {
+            const int r = m0q + lane;
+            const int p = r < a.M ? a.pos[r] : 0;  // rows past M are computed but their stores are clipped
+            const float4* src = reinterpret_cast<const float4*>(a.rope + (size_t)p * 32);
+#pragma unroll
+            for (int i = 0; i < 16; i++) cs[i] = __ldg(src + i);
+        }
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 64) {
+            float x0[32], x1[32];
+            load_cols(tacc + half * HALF + c, x0);
+            load_cols(tacc + half * HALF + c + 32, x1);
+            const int col = col0 + c;
+            add_bias(x0, a.bias, col);
+            add_bias(x1, a.bias, col + 32);
+            if (rope) {
+                // rotate_half pairing (d, d+32) within the head, src/main.zig:2512-2519
+#pragma unroll
+                for (int d = 0; d < 32; d += 2) {
+                    const float4 t = cs[d / 2];  // (cos d, sin d, cos d+1, sin d+1)
+                    const float a0 = x0[d], b0 = x1[d], a1 = x0[d + 1], b1 = x1[d + 1];
+                    x0[d] = a0 * t.x - b0 * t.y;
+                    x1[d] = b0 * t.x + a0 * t.y;
+                    x0[d + 1] = a1 * t.z - b1 * t.w;
+                    x1[d + 1] = b1 * t.z + a1 * t.w;
+                }
+            }
+            reuse_stage(lane);
+            stage16<T>(tile, lane, 0, x0);
+            stage16<T>(tile, lane, 4, x1);
+            flush_stage<false>(out_map, tile, lane, col, m0q);
+        }
+    } else if constexpr (EPI == EPI_F32 || EPI == EPI_RESID) {
 #pragma unroll 1
         for (int c = 0; c < HALF; c += 32) {
-            float g[32], u[32];
-            load_cols(tacc + c, g);
-            load_cols(tacc + HALF + c, u);
-            if (live) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) g[i] = gelu_as(g[i]) * u[i];
-                store16x32<T>(reinterpret_cast<T*>(a.out16) + (size_t)row * a.ldo + n_blk * HALF + c, g);
-            }
-        }
-    } else if constexpr (EPI == EPI_QKV) {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 64) {
-            float x0[32], x1[32];
-            load_cols(tacc + c, x0);
-            load_cols(tacc + c + 32, x1);
-            const int col = n_blk * BN + c;
-            if (live) {
-                add_bias(x0, a.bias, col);
-                add_bias(x1, a.bias, col + 32);
-                if (col < a.rope_cols) {
-                    // rotate_half pairing (d, d+32) within the head, src/main.zig:2512-2519
-                    const float4* cs = reinterpret_cast<const float4*>(a.rope + (size_t)a.pos[row] * 32);
-#pragma unroll
-                    for (int d = 0; d < 32; d += 2) {
-                        const float4 t = __ldg(cs + d / 2);  // (cos d, sin d, cos d+1, sin d+1)
-                        const float a0 = x0[d], b0 = x1[d], a1 = x0[d + 1], b1 = x1[d + 1];
-                        x0[d] = a0 * t.x - b0 * t.y;
-                        x1[d] = b0 * t.x + a0 * t.y;
-                        x0[d + 1] = a1 * t.z - b1 * t.w;
-                        x1[d + 1] = b1 * t.z + a1 * t.w;
-                    }
-                }
-                T* dst = reinterpret_cast<T*>(a.out16) + (size_t)row * a.ldo + col;
-                store16x32<T>(dst, x0);
-                store16x32<T>(dst + 32, x1);
-            }
-        }
-    } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
             float v[32];
-            load_cols(tacc + c, v);
-            const int col = n_blk * BN + c;
-            if (!live) continue;
+            load_cols(tacc + half * HALF + c, v);
+            const int col = n_blk * BN + half * HALF + c;
             add_bias(v, a.bias, col);
-            if constexpr (EPI == EPI_F32 || EPI == EPI_RESID) {
-                float4* dst = reinterpret_cast<float4*>(a.out_f32 + (size_t)row * a.ldo + col);
+            reuse_stage(lane);
+            stage32(tile, lane, v);
+            flush_stage<EPI == EPI_RESID>(out_map, tile, lane, col, m0q);
+        }
+    } else {  // EPI_ACT16, EPI_RELU
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 64) {
+            float x0[32], x1[32];
+            load_cols(tacc + half * HALF + c, x0);
+            load_cols(tacc + half * HALF + c + 32, x1);
+            const int col = n_blk * BN + half * HALF + c;
+            add_bias(x0, a.bias, col);
+            add_bias(x1, a.bias, col + 32);
+            if constexpr (EPI == EPI_RELU) {
 #pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                    if constexpr (EPI == EPI_RESID) {
-                        const float4 r = dst[q];
-                        o.x += r.x;
-                        o.y += r.y;
-                        o.z += r.z;
-                        o.w += r.w;
-                    }
-                    dst[q] = o;
+                for (int i = 0; i < 32; i++) {
+                    x0[i] = fmaxf(x0[i], 0.0f);
+                    x1[i] = fmaxf(x1[i], 0.0f);
                 }
-            } else {
-                if constexpr (EPI == EPI_RELU) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = fmaxf(v[i], 0.0f);
-                }
-                store16x32<T>(reinterpret_cast<T*>(a.out16) + (size_t)row * a.ldo + col, v);
             }
+            reuse_stage(lane);
+            stage16<T>(tile, lane, 0, x0);
+            stage16<T>(tile, lane, 4, x1);
+            flush_stage<false>(out_map, tile, lane, col, m0q);
         }
     }
 }
 
 template <int BN, int EPI, typename T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map, GemmArgs args) {
+    gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
+                const __grid_constant__ CUtensorMap out_map, GemmArgs args) {
     using C = Cfg<BN>;
     constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint8_t* staging = smem + C::RING;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + EPI_WARPS * STAGING_BYTES);
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + 2;
@@ -200,7 +256,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4);
+            mbar_init(&tempty[b], EPI_WARPS);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -210,6 +266,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&a_map);
         prefetch_tmap(&b_map);
+        prefetch_tmap(&out_map);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -299,7 +356,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __syncwarp();
     } else {
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int e = warp - 2;
+        const int q = warp & 3;          // TMEM lane quarter this warp may access
+        const int half = e >> 2;         // which half of the tile's columns
+        uint8_t* tile = staging + e * STAGING_BYTES;
         int it = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
             const int buf = it & 1;
@@ -309,13 +369,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const int row = (t / tiles_n) * BM + q * 32 + lane;
+            const int m0q = (t / tiles_n) * BM + q * 32;
             const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-            epilogue_tile<BN, EPI, T>(args, tacc, row, t % tiles_n);
+            epilogue_tile<BN, EPI, T>(args, &out_map, tile, tacc, half, lane, m0q, t % tiles_n);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
         }
+        if (lane == 0) bulk_wait_all();  // this warp's stores are complete before the CTA exits
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -342,52 +404,73 @@ cudaError_t prepare_bn() {
 }
 
 template <int BN, int EPI, typename T>
-cudaError_t launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const GemmArgs& args, int num_sms,
-                       cudaStream_t stream) {
+cudaError_t launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const CUtensorMap& out_map,
+                       const GemmArgs& args, int num_sms, cudaStream_t stream) {
     using C = Cfg<BN>;
     const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     if (grid <= 0) return cudaSuccess;
-    gemm_kernel<BN, EPI, T><<<grid, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, args);
+    gemm_kernel<BN, EPI, T><<<grid, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, out_map, args);
     return cudaGetLastError();
 }
 
 template <int BN, typename T>
-cudaError_t dispatch_epi(int epi, const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int sms,
-                         cudaStream_t s) {
+cudaError_t dispatch_epi(int epi, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                         const GemmArgs& args, int sms, cudaStream_t s) {
     switch (epi) {
-        case EPI_F32: return launch_one<BN, EPI_F32, T>(a, b, args, sms, s);
-        case EPI_ACT16: return launch_one<BN, EPI_ACT16, T>(a, b, args, sms, s);
-        case EPI_QKV: return launch_one<BN, EPI_QKV, T>(a, b, args, sms, s);
-        case EPI_RESID: return launch_one<BN, EPI_RESID, T>(a, b, args, sms, s);
-        case EPI_GLU: return launch_one<BN, EPI_GLU, T>(a, b, args, sms, s);
-        case EPI_RELU: return launch_one<BN, EPI_RELU, T>(a, b, args, sms, s);
+        case EPI_F32: return launch_one<BN, EPI_F32, T>(a, b, o, args, sms, s);
+        case EPI_ACT16: return launch_one<BN, EPI_ACT16, T>(a, b, o, args, sms, s);
+        case EPI_QKV: return launch_one<BN, EPI_QKV, T>(a, b, o, args, sms, s);
+        case EPI_RESID: return launch_one<BN, EPI_RESID, T>(a, b, o, args, sms, s);
+        case EPI_GLU: return launch_one<BN, EPI_GLU, T>(a, b, o, args, sms, s);
+        case EPI_RELU: return launch_one<BN, EPI_RELU, T>(a, b, o, args, sms, s);
     }
     return cudaErrorInvalidValue;
 }
 
-}  // namespace
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-CUresult make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
-                      bool bf16) {
-    using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeFn encoder() {
     static EncodeFn encode = nullptr;
     if (!encode) {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
             q != cudaDriverEntryPointSuccess || !fn)
-            return CUDA_ERROR_NOT_FOUND;
+            return nullptr;
         encode = reinterpret_cast<EncodeFn>(fn);
     }
+    return encode;
+}
+
+}  // namespace
+
+CUresult make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
+                      bool bf16) {
+    EncodeFn encode = encoder();
+    if (!encode) return CUDA_ERROR_NOT_FOUND;
     const cuuint64_t dims[2] = {inner, rows};
     const cuuint64_t strides[1] = {inner * 2};
     const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+CUresult make_out_map(CUtensorMap* map, void* base, uint64_t inner, uint64_t rows, int elem_bytes, bool bf16) {
+    EncodeFn encode = encoder();
+    if (!encode) return CUDA_ERROR_NOT_FOUND;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : bf16          ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return encode(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
@@ -406,14 +489,15 @@ cudaError_t gemm_prepare() {
 }
 
 cudaError_t launch_gemm(int epi, int bn, bool bf16, const CUtensorMap& a_map, const CUtensorMap& b_map,
-                        const GemmArgs& args, int num_sms, cudaStream_t stream) {
+                        const CUtensorMap& out_map, const GemmArgs& args, int num_sms, cudaStream_t stream) {
     if (args.K % BK || args.N % bn || args.M < 0) return cudaErrorInvalidValue;
+    if ((epi == EPI_GLU || epi == EPI_QKV) && bn != 256) return cudaErrorInvalidValue;
     if (bn == 256)
-        return bf16 ? dispatch_epi<256, __nv_bfloat16>(epi, a_map, b_map, args, num_sms, stream)
-                    : dispatch_epi<256, __half>(epi, a_map, b_map, args, num_sms, stream);
+        return bf16 ? dispatch_epi<256, __nv_bfloat16>(epi, a_map, b_map, out_map, args, num_sms, stream)
+                    : dispatch_epi<256, __half>(epi, a_map, b_map, out_map, args, num_sms, stream);
     if (bn == 128)
-        return bf16 ? dispatch_epi<128, __nv_bfloat16>(epi, a_map, b_map, args, num_sms, stream)
-                    : dispatch_epi<128, __half>(epi, a_map, b_map, args, num_sms, stream);
+        return bf16 ? dispatch_epi<128, __nv_bfloat16>(epi, a_map, b_map, out_map, args, num_sms, stream)
+                    : dispatch_epi<128, __half>(epi, a_map, b_map, out_map, args, num_sms, stream);
     return cudaErrorInvalidValue;
 }
 

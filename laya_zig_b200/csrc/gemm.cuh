@@ -21,9 +21,6 @@ enum Epilogue : int {
 struct GemmArgs {
     int M, N, K;
     const float* bias;      // [N] or null
-    float* out_f32;         // EPI_F32 / EPI_RESID
-    void* out16;            // 16-bit outputs (type = the GEMM's element type)
-    int ldo;                // output row stride in elements
     const int* pos;         // EPI_QKV: RoPE position of each row
     const float2* rope;     // EPI_QKV: [MAX_POS][32] (cos, sin)
     int rope_cols;          // EPI_QKV: RoPE applies to columns [0, rope_cols)
@@ -31,9 +28,16 @@ struct GemmArgs {
 };
 
 // 2-D tensor map over a row-major [rows][inner] 16-bit matrix, box
-// [box_rows][64] with 128-byte swizzle (the UMMA K-major SW128 layout).
+// [box_rows][64] with 128-byte swizzle: the operand layout of the GEMM
+// (UMMA K-major, SWIZZLE_128B).
 CUresult make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
                       bool bf16);
+
+// Output tensor map of an epilogue: [rows][inner] row-major, elements of
+// `elem_bytes` (2: 16-bit of the GEMM's type, 4: f32), box of 32 rows x
+// 128 bytes with 128-byte swizzle. The epilogue writes it with TMA stores
+// (EPI_RESID: TMA reduce-add). Rows at or past `rows` are never written.
+CUresult make_out_map(CUtensorMap* map, void* base, uint64_t inner, uint64_t rows, int elem_bytes, bool bf16);
 
 // Raise the dynamic shared-memory limit of every GEMM instantiation on the
 // current device (once per device; must not run during stream capture).
@@ -42,6 +46,6 @@ cudaError_t gemm_prepare();
 // Launch one GEMM. BN (128 or 256) must divide N, 64 must divide K.
 // A's map has box rows 128, B's map box rows BN. Returns a CUDA error code.
 cudaError_t launch_gemm(int epi, int bn, bool bf16, const CUtensorMap& a_map, const CUtensorMap& b_map,
-                        const GemmArgs& args, int num_sms, cudaStream_t stream);
+                        const CUtensorMap& out_map, const GemmArgs& args, int num_sms, cudaStream_t stream);
 
 }  // namespace laya

@@ -92,7 +92,6 @@ struct laya_ctx {
     uint32_t* d_mk = nullptr;
     int* d_cum = nullptr;
     float *d_logits = nullptr, *d_act = nullptr, *d_pooled = nullptr;
-    CUtensorMap m_xn, m_ctx, m_mlp, m_ff;
     int* d_err = nullptr;
     int* h_err = nullptr;  // pinned
     void* h_stage = nullptr;
@@ -217,11 +216,6 @@ int ensure_workspace(laya_ctx* c, int M, int S, int G) {
     c->capM = nM;
     c->capS = nS;
     c->capG = nG;
-    CUresult r = make_tmap_2d(&c->m_xn, c->xn, D, nM, 128, c->bf16);
-    if (r == CUDA_SUCCESS) r = make_tmap_2d(&c->m_ctx, c->ctxb, D, nM, 128, c->bf16);
-    if (r == CUDA_SUCCESS) r = make_tmap_2d(&c->m_mlp, c->mlp, INTER, nM, 128, c->bf16);
-    if (r == CUDA_SUCCESS) r = make_tmap_2d(&c->m_ff, c->ff, HEAD_FF, nM, 128, c->bf16);
-    if (r != CUDA_SUCCESS) return fail(c, LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     const size_t stage = (size_t)nM * 4 + (size_t)(nS + 1) * 8 + (size_t)nS * 4 + (size_t)nG * 4 + 64 +
                          (size_t)nG * 4 + (size_t)nS * 8;
     if (stage > c->h_stage_bytes) {
@@ -246,27 +240,44 @@ struct Outs {
     float *logits, *act, *pooled, *hidden;
 };
 
-cudaError_t gemm(laya_ctx* c, int epi, const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K,
-                 const float* bias, float* out_f32, void* out16, int ldo, int rope_cols, cudaStream_t s) {
+// Tensor maps over the workspace for a batch of exactly M tokens: GEMM
+// operand loads (zero-filled past M) and epilogue stores (clipped at M).
+struct ActMaps {
+    CUtensorMap a_xn, a_ctx, a_mlp, a_ff;  // A operands, box 128 x 64
+    CUtensorMap o_qkv, o_mlp, o_ff, o_x;   // outputs, box 32 rows x 128 bytes
+};
+
+int build_maps(laya_ctx* c, int M, ActMaps* m) {
+    CUresult r = make_tmap_2d(&m->a_xn, c->xn, D, M, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&m->a_ctx, c->ctxb, D, M, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&m->a_mlp, c->mlp, INTER, M, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&m->a_ff, c->ff, HEAD_FF, M, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_out_map(&m->o_qkv, c->qkv, 3 * D, M, 2, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_out_map(&m->o_mlp, c->mlp, INTER, M, 2, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_out_map(&m->o_ff, c->ff, HEAD_FF, M, 2, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_out_map(&m->o_x, c->x, D, M, 4, c->bf16);
+    if (r != CUDA_SUCCESS) return fail(c, LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return LAYA_OK;
+}
+
+cudaError_t gemm(laya_ctx* c, int epi, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& out, int M,
+                 int N, int K, const float* bias, int rope_cols, cudaStream_t s) {
     GemmArgs g{};
     g.M = M;
     g.N = N;
     g.K = K;
     g.bias = bias;
-    g.out_f32 = out_f32;
-    g.out16 = out16;
-    g.ldo = ldo;
     g.pos = c->pos;
     g.rope = c->rope;
     g.rope_cols = rope_cols;
     g.err = c->d_err;
-    return launch_gemm(epi, 256, c->bf16, a, b, g, c->num_sms, s);
+    return launch_gemm(epi, 256, c->bf16, a, b, out, g, c->num_sms, s);
 }
 
 // The whole forward on stream `s`. The hook sees begin(stage)/end(stage)
 // around every kernel launch and tap(tag) after each --dumpstats point.
 template <typename Hook>
-cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t s, Hook& hook) {
+cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMaps& am, cudaStream_t s, Hook& hook) {
     cudaError_t e;
 #define RUN(stage, x)                           \
     do {                                        \
@@ -283,14 +294,14 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t
         const EncW& w = c->enc[l];
         if (w.attn_norm) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.attn_norm, nullptr, M, s));
         RUN(LAYA_STAGE_GEMM_QKV,
-            gemm(c, EPI_QKV, c->m_xn, w.m_qkv, M, 3 * D, D, nullptr, nullptr, c->qkv, 3 * D, 2 * D, s));
+            gemm(c, EPI_QKV, am.a_xn, w.m_qkv, am.o_qkv, M, 3 * D, D, nullptr, 2 * D, s));
         RUN(LAYA_STAGE_ATTN,
             launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, (l % 3) ? WINDOW : -1, s));
-        RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, c->m_ctx, w.m_wo, M, D, D, nullptr, c->x, nullptr, D, 0, s));
+        RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_wo, am.o_x, M, D, D, nullptr, 0, s));
         RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.mlp_norm, nullptr, M, s));
         RUN(LAYA_STAGE_GEMM_UP,
-            gemm(c, EPI_GLU, c->m_xn, w.m_wi, M, 2 * INTER, D, nullptr, nullptr, c->mlp, INTER, 0, s));
-        RUN(LAYA_STAGE_GEMM_DOWN, gemm(c, EPI_RESID, c->m_mlp, w.m_wo2, M, D, INTER, nullptr, c->x, nullptr, D, 0, s));
+            gemm(c, EPI_GLU, am.a_xn, w.m_wi, am.o_mlp, M, 2 * INTER, D, nullptr, 0, s));
+        RUN(LAYA_STAGE_GEMM_DOWN, gemm(c, EPI_RESID, am.a_mlp, w.m_wo2, am.o_x, M, D, INTER, nullptr, 0, s));
         hook.tap(1 + l);
     }
     RUN(LAYA_STAGE_FINAL, launch_final(c->bf16, c->x, c->xn, c->final_norm, c->type_emb, b.qt, c->seq_of,
@@ -299,14 +310,14 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t
     for (int l = 0; l < HEAD_LAYERS; l++) {
         const HeadW& w = c->head[l];
         if (l > 0) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n1w, w.n1b, M, s));
-        RUN(LAYA_STAGE_GEMM_QKV, gemm(c, EPI_QKV, c->m_xn, w.m_in, M, 3 * D, D, w.in_b, nullptr, c->qkv, 3 * D, 0, s));
+        RUN(LAYA_STAGE_GEMM_QKV, gemm(c, EPI_QKV, am.a_xn, w.m_in, am.o_qkv, M, 3 * D, D, w.in_b, 0, s));
         RUN(LAYA_STAGE_ATTN, launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, -1, s));
-        RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, c->m_ctx, w.m_out, M, D, D, w.out_b, c->x, nullptr, D, 0, s));
+        RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_out, am.o_x, M, D, D, w.out_b, 0, s));
         RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n2w, w.n2b, M, s));
         RUN(LAYA_STAGE_GEMM_UP,
-            gemm(c, EPI_RELU, c->m_xn, w.m_l1, M, HEAD_FF, D, w.l1_b, nullptr, c->ff, HEAD_FF, 0, s));
+            gemm(c, EPI_RELU, am.a_xn, w.m_l1, am.o_ff, M, HEAD_FF, D, w.l1_b, 0, s));
         RUN(LAYA_STAGE_GEMM_DOWN,
-            gemm(c, EPI_RESID, c->m_ff, w.m_l2, M, D, HEAD_FF, w.l2_b, c->x, nullptr, D, 0, s));
+            gemm(c, EPI_RESID, am.a_ff, w.m_l2, am.o_x, M, D, HEAD_FF, w.l2_b, 0, s));
         hook.tap(25 + l);
     }
     RUN(LAYA_STAGE_TAIL, launch_tail(c->x, b.cu, b.mk, b.cum, b.S, b.G, c->tail, c->mv, c->partial, o.logits, o.act,
@@ -422,9 +433,12 @@ int launch_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t s) {
             c->graphs.clear();
         }
         cudaGraph_t graph;
-        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        ActMaps am;
+        int rc = build_maps(c, b.M, &am);
+        if (rc) return rc;
         NoHook hook;
-        cudaError_t e = run_forward(c, b, o, c->stream, hook);
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = run_forward(c, b, o, am, c->stream, hook);
         cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
         if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "launch during capture: %s", cudaGetErrorString(e));
         if (e2 != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(e2));
@@ -758,8 +772,11 @@ int laya_gpu_forward_trace(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_
     if (rc) return rc;
     Outs o{c->d_logits, c->d_act, nullptr, nullptr};
     const size_t LD = (size_t)L * D;
+    ActMaps am;
+    rc = build_maps(c, M, &am);
+    if (rc) return rc;
     TraceHook hook{c, trace, LD};
-    cudaError_t e = run_forward(c, b, o, c->stream, hook);
+    cudaError_t e = run_forward(c, b, o, am, c->stream, hook);
     if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
     CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
     if (G) CK(cudaMemcpyAsync(logits, c->d_logits, (size_t)G * 4, cudaMemcpyDeviceToHost, c->stream));
@@ -789,8 +806,11 @@ int laya_gpu_forward_dump(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t
     rc = stage_batch(c, &sq, 1, M, G, maxlen, &b);
     if (rc) return rc;
     Outs o{c->d_logits, c->d_act, nullptr, nullptr};
+    ActMaps am;
+    rc = build_maps(c, M, &am);
+    if (rc) return rc;
     DumpHook hook{c, layer, M, xn_attn, qkv, ctx_out, xn_mlp, glu, x_mid};
-    cudaError_t e = run_forward(c, b, o, c->stream, hook);
+    cudaError_t e = run_forward(c, b, o, am, c->stream, hook);
     if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
     CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
@@ -811,11 +831,14 @@ int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, f
             (int)bt->n_markers, (int)bt->max_len};
     Outs o{logits, act, nullptr, nullptr};
     for (int i = 0; i < LAYA_N_STAGES; i++) stage_ms[i] = 0.f;
+    ActMaps am;
+    rc = build_maps(c, (int)bt->n_tokens, &am);
+    if (rc) return rc;
     ProfileHook hook;
     hook.s = s;
     for (int it = 0; it < iters; it++) {
         for (int i = 0; i < LAYA_N_STAGES; i++) hook.launches[i] = 0;
-        cudaError_t e = run_forward(c, b, o, s, hook);
+        cudaError_t e = run_forward(c, b, o, am, s, hook);
         if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile forward: %s", cudaGetErrorString(e));
         CK(cudaStreamSynchronize(s));
         hook.collect(stage_ms);
@@ -847,18 +870,17 @@ int laya_gpu_linear(const void* x, const void* w, const float* bias, float* out,
         CK(cudaMemset(d_err[dev], 0, 4));
         CK(cudaDeviceSynchronize());  // the launch below may be on a stream that does not wait on this one
     }
-    CUtensorMap am, bm;
-    if (make_tmap_2d(&am, x, K, M, 128, bf16) != CUDA_SUCCESS || make_tmap_2d(&bm, w, K, N, bn, bf16) != CUDA_SUCCESS)
+    CUtensorMap am, bm, om;
+    if (make_tmap_2d(&am, x, K, M, 128, bf16) != CUDA_SUCCESS || make_tmap_2d(&bm, w, K, N, bn, bf16) != CUDA_SUCCESS ||
+        make_out_map(&om, out, N, M, 4, bf16) != CUDA_SUCCESS)
         return fail(c, LAYA_ERR_CUDA, "linear: cuTensorMapEncodeTiled failed");
     GemmArgs g{};
     g.M = M;
     g.N = N;
     g.K = K;
     g.bias = bias;
-    g.out_f32 = out;
-    g.ldo = N;
     g.err = d_err[dev < 64 ? dev : 0];
-    CK(launch_gemm(EPI_F32, bn, bf16, am, bm, g, sms, static_cast<cudaStream_t>(stream)));
+    CK(launch_gemm(EPI_F32, bn, bf16, am, bm, om, g, sms, static_cast<cudaStream_t>(stream)));
     return LAYA_OK;
 }
 
