@@ -34,12 +34,13 @@ constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int STAGING_BYTES = 32 * 128;  // one 32-row x 128-byte output tile per epilogue warp
 
-template <int BN>
+template <int BN, bool PAIR = false>
 struct Cfg {
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B rows this CTA loads per tile
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int STAGES = (STAGE_BYTES >= 48 * 1024) ? 4 : 6;
     static constexpr int RING = STAGES * STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // two accumulators of BN f32 columns
     static constexpr int SMEM = RING + EPI_WARPS * STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
@@ -225,12 +226,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
     }
 }
 
-template <int BN, int EPI, typename T>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
-                const __grid_constant__ CUtensorMap out_map, GemmArgs args) {
-    using C = Cfg<BN>;
-    constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+// PAIR: a cluster of two CTAs computes a 256 x BN tile with cta_group::2
+// MMAs issued by rank 0; each CTA loads its own 128 A rows and BN/2 B rows,
+// holds its 128 accumulator rows in its own TMEM and runs its own epilogue.
+template <int BN, int EPI, typename T, bool PAIR>
+__device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtensorMap& b_map,
+                                          const CUtensorMap& out_map, const GemmArgs& args) {
+    using C = Cfg<BN, PAIR>;
+    constexpr int TILE_M = PAIR ? 2 * BM : BM;
+    constexpr uint32_t IDESC = idesc_f16(TILE_M, BN, std::is_same<T, __nv_bfloat16>::value);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + C::RING;
@@ -244,7 +248,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int tiles_m = (args.M + BM - 1) / BM;
+    const uint32_t rank = PAIR ? cluster_rank() : 0;
+    const bool leader = rank == 0;
+    const int unit = PAIR ? (blockIdx.x >> 1) : blockIdx.x;       // this CTA's (pair's) index
+    const int units = PAIR ? (gridDim.x >> 1) : gridDim.x;
+    const int tiles_m = (args.M + TILE_M - 1) / TILE_M;
     const int tiles_n = args.N / BN;
     const int total = tiles_m * tiles_n;
     const int nk = args.K / BK;
@@ -256,7 +264,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], EPI_WARPS);
+            mbar_init(&tempty[b], PAIR ? 2 * EPI_WARPS : EPI_WARPS);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -269,11 +277,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         prefetch_tmap(&out_map);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before anyone signals them
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -283,14 +297,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t phase = 0;
             int issued_phase[C::STAGES];
             for (int s = 0; s < C::STAGES; s++) issued_phase[s] = -1;
-            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+            for (int t = unit; t < total && !*abort_flag; t += units) {
+                const int m0 = (t / tiles_n) * TILE_M + (int)rank * BM;
+                const int n0 = (t % tiles_n) * BN + (int)rank * C::B_ROWS;
                 for (int kb = 0; kb < nk; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, args.err, abort_flag)) goto producer_done;
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-                    tma_load_2d(sa, &a_map, &full[stage], kb * BK, m0);
-                    tma_load_2d(sa + C::A_BYTES, &b_map, &full[stage], kb * BK, n0);
+                    if constexpr (PAIR) {
+                        // both CTAs' bytes complete on rank 0's barrier; only rank 0 arms it
+                        const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+                        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+                        tma_load_2d_pair(sa, &a_map, bar, kb * BK, m0);
+                        tma_load_2d_pair(sa + C::A_BYTES, &b_map, bar, kb * BK, n0);
+                    } else {
+                        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                        tma_load_2d(sa, &a_map, &full[stage], kb * BK, m0);
+                        tma_load_2d(sa + C::A_BYTES, &b_map, &full[stage], kb * BK, n0);
+                    }
                     issued_phase[stage] = (int)phase;
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -299,11 +322,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
         producer_done:
-            // Let every load this thread issued land before shared memory goes away.
+            // Let every load this thread issued land before shared memory goes
+            // away. In a pair the completions are counted on rank 0's barrier;
+            // this CTA's empty barrier flips only after rank 0 consumed them.
             for (int s = 0; s < C::STAGES; s++) {
                 if (issued_phase[s] < 0) continue;
+                uint64_t* bar = PAIR ? &empty[s] : &full[s];
                 const unsigned long long t0 = globaltimer();
-                while (!mbar_try_wait(&full[s], (uint32_t)issued_phase[s])) {
+                while (!mbar_try_wait(bar, (uint32_t)issued_phase[s])) {
                     if (globaltimer() - t0 > WAIT_LIMIT_NS) {
                         atomicOr(args.err, ERR_WAIT_TIMEOUT);
                         break;
@@ -313,11 +339,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && leader) {
             int stage = 0;
             uint32_t phase = 0;
             int it = 0;
-            for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
+            for (int t = unit; t < total; t += units, it++) {
                 const int buf = it & 1;
                 const uint32_t tph = (it >> 1) & 1;
                 if (!mbar_wait(&tempty[buf], tph ^ 1, args.err, abort_flag)) break;
@@ -333,19 +359,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
                     const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + C::A_BYTES);
 #pragma unroll
-                    for (int k = 0; k < BK / 16; k++)
-                        tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
-                    tc_commit(&empty[stage]);
+                    for (int k = 0; k < BK / 16; k++) {
+                        if constexpr (PAIR) tc_mma_f16_pair(d, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
+                        else tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
+                    }
+                    if constexpr (PAIR) tc_commit_pair(&empty[stage], 0x3);
+                    else tc_commit(&empty[stage]);
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
-                tc_commit(&tfull[buf]);
+                if constexpr (PAIR) tc_commit_pair(&tfull[buf], 0x3);
+                else tc_commit(&tfull[buf]);
             }
             // All MMAs this thread issued are complete once `drain` flips.
-            tc_commit(drain);
+            if constexpr (PAIR) tc_commit_pair(drain, 0x1);
+            else tc_commit(drain);
             const unsigned long long t0 = globaltimer();
             while (!mbar_try_wait(drain, 0)) {
                 if (globaltimer() - t0 > WAIT_LIMIT_NS) {
@@ -360,8 +391,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int q = warp & 3;          // TMEM lane quarter this warp may access
         const int half = e >> 2;         // which half of the tile's columns
         uint8_t* tile = staging + e * STAGING_BYTES;
+        const uint32_t tempty_leader = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0;
         int it = 0;
-        for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
+        for (int t = unit; t < total; t += units, it++) {
             const int buf = it & 1;
             const uint32_t tph = (it >> 1) & 1;
             int ok = 1;
@@ -369,26 +401,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const int m0q = (t / tiles_n) * BM + q * 32;
+            const int m0q = (t / tiles_n) * TILE_M + (int)rank * BM + q * 32;
             const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
             epilogue_tile<BN, EPI, T>(args, &out_map, tile, tacc, half, lane, m0q, t % tiles_n);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
+            if (lane == 0) {
+                if constexpr (PAIR) mbar_arrive_cluster(tempty_leader + buf * 8);
+                else mbar_arrive(&tempty[buf]);
+            }
         }
         if (lane == 0) bulk_wait_all();  // this warp's stores are complete before the CTA exits
         __syncwarp();
     }
 
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // neither CTA frees TMEM while the pair may still use it
+    else __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (warp == 1) {
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        else tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+template <int BN, int EPI, typename T>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
+                const __grid_constant__ CUtensorMap out_map, GemmArgs args) {
+    gemm_body<BN, EPI, T, false>(a_map, b_map, out_map, args);
+}
+
+template <int EPI, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
+                     const __grid_constant__ CUtensorMap out_map, GemmArgs args) {
+    gemm_body<256, EPI, T, true>(a_map, b_map, out_map, args);
 }
 
 template <int BN, int EPI, typename T>
 cudaError_t prepare_one() {
-    return cudaFuncSetAttribute(gemm_kernel<BN, EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+    if constexpr (BN == 256)
+        return cudaFuncSetAttribute(gemm_pair_kernel<EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg<256, true>::SMEM);
+    else
+        return cudaFuncSetAttribute(gemm_kernel<BN, EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg<BN>::SMEM);
 }
 
 template <int BN, typename T>
@@ -403,14 +461,23 @@ cudaError_t prepare_bn() {
     return e;
 }
 
+// BN = 256: CTA pairs (cluster of 2, 256 x 256 tiles); BN = 128: single CTAs.
 template <int BN, int EPI, typename T>
 cudaError_t launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const CUtensorMap& out_map,
                        const GemmArgs& args, int num_sms, cudaStream_t stream) {
-    using C = Cfg<BN>;
-    const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
-    const int grid = tiles < num_sms ? tiles : num_sms;
-    if (grid <= 0) return cudaSuccess;
-    gemm_kernel<BN, EPI, T><<<grid, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, out_map, args);
+    if constexpr (BN == 256) {
+        using C = Cfg<256, true>;
+        const int tiles = ((args.M + 2 * BM - 1) / (2 * BM)) * (args.N / BN);
+        const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+        if (pairs <= 0) return cudaSuccess;
+        gemm_pair_kernel<EPI, T><<<2 * pairs, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, out_map, args);
+    } else {
+        using C = Cfg<BN>;
+        const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
+        const int grid = tiles < num_sms ? tiles : num_sms;
+        if (grid <= 0) return cudaSuccess;
+        gemm_kernel<BN, EPI, T><<<grid, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, out_map, args);
+    }
     return cudaGetLastError();
 }
 

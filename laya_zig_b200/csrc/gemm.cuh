@@ -44,7 +44,9 @@ CUresult make_out_map(CUtensorMap* map, void* base, uint64_t inner, uint64_t row
 cudaError_t gemm_prepare();
 
 // Launch one GEMM. BN (128 or 256) must divide N, 64 must divide K.
-// A's map has box rows 128, B's map box rows BN. Returns a CUDA error code.
+// BN = 256 runs CTA pairs (256 x 256 tiles, cta_group::2), BN = 128 single
+// CTAs (128 x 128). A's and B's maps both have 128-row boxes. Returns a CUDA
+// error code.
 cudaError_t launch_gemm(int epi, int bn, bool bf16, const CUtensorMap& a_map, const CUtensorMap& b_map,
                         const CUtensorMap& out_map, const GemmArgs& args, int num_sms, cudaStream_t stream);
 

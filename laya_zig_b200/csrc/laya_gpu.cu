@@ -170,7 +170,7 @@ int upload(laya_ctx* c, const laya_tensor* t, int n, const char* name, uint64_t 
 }
 
 int weight_map(laya_ctx* c, CUtensorMap* m, const void* w, uint64_t rows, uint64_t cols) {
-    CUresult r = make_tmap_2d(m, w, cols, rows, 256, c->bf16);
+    CUresult r = make_tmap_2d(m, w, cols, rows, 128, c->bf16);  // B operand box: 128 rows
     if (r != CUDA_SUCCESS) return fail(c, LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return LAYA_OK;
 }
@@ -871,7 +871,7 @@ int laya_gpu_linear(const void* x, const void* w, const float* bias, float* out,
         CK(cudaDeviceSynchronize());  // the launch below may be on a stream that does not wait on this one
     }
     CUtensorMap am, bm, om;
-    if (make_tmap_2d(&am, x, K, M, 128, bf16) != CUDA_SUCCESS || make_tmap_2d(&bm, w, K, N, bn, bf16) != CUDA_SUCCESS ||
+    if (make_tmap_2d(&am, x, K, M, 128, bf16) != CUDA_SUCCESS || make_tmap_2d(&bm, w, K, N, 128, bf16) != CUDA_SUCCESS ||
         make_out_map(&om, out, N, M, 4, bf16) != CUDA_SUCCESS)
         return fail(c, LAYA_ERR_CUDA, "linear: cuTensorMapEncodeTiled failed");
     GemmArgs g{};

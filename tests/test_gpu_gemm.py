@@ -80,6 +80,16 @@ def test_selftest_shapes_uniform(rows, n, k):
     assert _check(out, _to_f64(xb), _to_f64(wb), every=1) < (1e-4 if k <= 1152 else 2e-4)
 
 
+@pytest.mark.parametrize("rows,n,k", [(200, 384, 768), (1000, 640, 1152)])
+def test_single_cta_path(rows, n, k):
+    """N not a multiple of 256 runs single CTAs (128 x 128 tiles) instead of CTA pairs."""
+    rng = np.random.default_rng(rows + n)
+    xb = _rand_bits(rng, (rows, k), 1.0)
+    wb = _rand_bits(rng, (n, k), 0.02)
+    out = _gpu_linear(xb, wb)
+    assert _check(out, _to_f64(xb), _to_f64(wb), every=1) < 1e-4
+
+
 def test_gemm_bias_and_f16():
     rng = np.random.default_rng(3)
     xb = _rand_bits(rng, (200, 768), 1.0, f16=True)
