@@ -26,6 +26,14 @@ constexpr int THREADS = 128;
 // are XOR-swizzled by row, so ldmatrix row fetches never share a bank.
 __device__ __forceinline__ int swz(int r, int c) { return r * 64 + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7); }
 
+// 2^x with the SFU's approximate exp2 (relative error ~2^-22; -inf -> 0),
+// far below the bf16 rounding P gets for the tensor-core P.V product.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
     const int sz = valid ? 16 : 0;
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(sz) : "memory");
@@ -95,7 +103,7 @@ __device__ __forceinline__ void load_tile(T* tile, const T* src, int ld, int r0,
 }
 
 template <typename T>
-__global__ void __launch_bounds__(THREADS) attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
+__global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
                                                             const int* __restrict__ cu_seqlens, int window) {
     __shared__ __align__(128) T sQ[QB * 64];
     __shared__ __align__(128) T sK[2][KB * 64];
@@ -163,37 +171,47 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const T* __restrict_
                 mma16816<T>(s[2 * np + 1], qa[ks], b[2], b[3]);
             }
         }
-        // mask + online softmax (two rows per thread: qi0 and qi1)
+        // Masks only on tiles that cross the sequence end or a window edge
+        // (keys j of the tile, rows i of the block: j < L and |i - j| <= window).
+        const int klo = kt * KB, khi = kt * KB + KB - 1;
+        const bool need_mask = khi >= L || (window >= 0 && (q0 + QB - 1 - klo > window || khi - q0 > window));
+        if (need_mask) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int kj = klo + j * 8 + 2 * (lane & 3) + e;
+                    const bool ok0 = kj < L && (window < 0 || abs(qi0 - kj) <= window);
+                    const bool ok1 = kj < L && (window < 0 || abs(qi1 - kj) <= window);
+                    if (!ok0) s[j][e] = -INFINITY;
+                    if (!ok1) s[j][2 + e] = -INFINITY;
+                }
+            }
+        }
+        // online softmax over raw scores, two rows per thread (qi0, qi1);
+        // p = 2^(s * log2(e)/8 - max * log2(e)/8)
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int kj = kt * KB + j * 8 + 2 * (lane & 3) + e;
-                const bool ok0 = kj < L && (window < 0 || abs(qi0 - kj) <= window);
-                const bool ok1 = kj < L && (window < 0 || abs(qi1 - kj) <= window);
-                s[j][e] = ok0 ? s[j][e] * sl2 : -INFINITY;
-                s[j][2 + e] = ok1 ? s[j][2 + e] * sl2 : -INFINITY;
-                mx0 = fmaxf(mx0, s[j][e]);
-                mx1 = fmaxf(mx1, s[j][2 + e]);
-            }
+            mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+            mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
         }
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
         const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-        const float u0 = n0 == -INFINITY ? 0.f : n0, u1 = n1 == -INFINITY ? 0.f : n1;
-        const float a0 = exp2f(m0 - u0), a1 = exp2f(m1 - u1);
+        const float u0 = n0 == -INFINITY ? 0.f : n0 * sl2, u1 = n1 == -INFINITY ? 0.f : n1 * sl2;
+        const float a0 = ex2(m0 * sl2 - u0), a1 = ex2(m1 * sl2 - u1);
         m0 = n0;
         m1 = n1;
         float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            s[j][0] = exp2f(s[j][0] - u0);
-            s[j][1] = exp2f(s[j][1] - u0);
-            s[j][2] = exp2f(s[j][2] - u1);
-            s[j][3] = exp2f(s[j][3] - u1);
+            s[j][0] = ex2(fmaf(s[j][0], sl2, -u0));
+            s[j][1] = ex2(fmaf(s[j][1], sl2, -u0));
+            s[j][2] = ex2(fmaf(s[j][2], sl2, -u1));
+            s[j][3] = ex2(fmaf(s[j][3], sl2, -u1));
             rs0 += s[j][0] + s[j][1];
             rs1 += s[j][2] + s[j][3];
         }

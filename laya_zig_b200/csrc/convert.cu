@@ -45,7 +45,20 @@ __global__ void convert_f32_kernel(float* dst, const void* src, int dtype, size_
         dst[i] = load_any(src, dtype, i);
 }
 
+__global__ void transpose_f32_kernel(float* dst, const float* src, int rows, int cols) {
+    const size_t n = (size_t)rows * cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / cols, c = i % cols;
+        dst[c * rows + r] = src[i];
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_transpose_f32(float* dst, const float* src, int rows, int cols, cudaStream_t s) {
+    transpose_f32_kernel<<<148 * 4, 256, 0, s>>>(dst, src, rows, cols);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_convert16(void* dst, bool dst_bf16, const void* src, int src_dtype, size_t rows, size_t cols,
                              int glu_tile, cudaStream_t s) {

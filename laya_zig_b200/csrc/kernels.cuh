@@ -15,7 +15,7 @@ cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const f
 // tail.cu ------------------------------------------------------------------
 struct TailWeights {
     const float *s0w, *s0b, *s1w, *s1b, *s3w, *s3b;  // scorer: LN, 768x768 + b, 1x768 + b
-    const float *a0w, *a0b, *a2w, *a2b;              // act head: 256x772 + b, 2x256 + b
+    const float *a0t, *a0b, *a2w, *a2b;              // act head: 772x256 (act_head.0.weight transposed) + b, 2x256 + b
 };
 constexpr int SCORER_GROUPS = D / 64;  // partial sums per marker, one per 64 scorer outputs
 constexpr int MAX_MARKERS_PER_SEQ = 1024;
@@ -32,5 +32,7 @@ cudaError_t launch_tail(const float* x, const int* cu_seqlens, const uint32_t* m
 cudaError_t launch_convert16(void* dst, bool dst_bf16, const void* src, int src_dtype, size_t rows, size_t cols,
                              int glu_tile, cudaStream_t s);
 cudaError_t launch_convert_f32(float* dst, const void* src, int src_dtype, size_t n, cudaStream_t s);
+// dst[cols][rows] = src[rows][cols]^T, f32.
+cudaError_t launch_transpose_f32(float* dst, const float* src, int rows, int cols, cudaStream_t s);
 
 }  // namespace laya

@@ -383,39 +383,44 @@ struct DumpHook {
     }
 };
 
-// An event pair around every launch; per-stage times summed after a sync.
+// An event pair around every launch. Recorded while the forward is being
+// captured, the events become external event-record nodes of the graph, so
+// the times are those of the graph's back-to-back kernels.
 struct ProfileHook {
     cudaStream_t s;
-    std::vector<cudaEvent_t> ev;
+    std::vector<cudaEvent_t> ev;  // created before capture
     std::vector<int> stage;
     size_t used = 0;
     int launches[LAYA_N_STAGES] = {0};
-    void begin(int st) {
-        if (used + 2 > ev.size()) {
-            cudaEvent_t a, b;
-            cudaEventCreate(&a);
-            cudaEventCreate(&b);
-            ev.push_back(a);
-            ev.push_back(b);
-            stage.push_back(st);
+    cudaError_t reserve(size_t pairs) {
+        while (ev.size() < 2 * pairs) {
+            cudaEvent_t e;
+            cudaError_t r = cudaEventCreate(&e);
+            if (r != cudaSuccess) return r;
+            ev.push_back(e);
         }
+        stage.resize(pairs);
+        return cudaSuccess;
+    }
+    void begin(int st) {
+        if (used + 2 > ev.size()) return;  // more launches than reserved: left untimed
         stage[used / 2] = st;
-        cudaEventRecord(ev[used], s);
+        cudaEventRecordWithFlags(ev[used], s, cudaEventRecordExternal);
     }
     void end(int st) {
-        cudaEventRecord(ev[used + 1], s);
-        used += 2;
         launches[st]++;
+        if (used + 2 > ev.size()) return;
+        cudaEventRecordWithFlags(ev[used + 1], s, cudaEventRecordExternal);
+        used += 2;
     }
     void tap(int) {}
     void extra(int st, int n) { launches[st] += n; }
-    void collect(float* stage_ms) {
+    void collect(float* stage_ms) const {
         for (size_t i = 0; i < used; i += 2) {
             float ms = 0.f;
             cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
             stage_ms[stage[i / 2]] += ms;
         }
-        used = 0;
     }
     ~ProfileHook() {
         for (cudaEvent_t e : ev) cudaEventDestroy(e);
@@ -625,7 +630,13 @@ int create_impl(laya_ctx* c, const laya_tensor* t, int n) {
     VEC("act_head.2.bias", 2, &a2b);
     cudaFree(staging);
     if (rc) return rc;
-    c->tail = TailWeights{s0w, s0b, s1w, s1b, s3w, s3b, a0w, a0b, a2w, a2b};
+    // the act head reads act_head.0.weight column-wise: keep it transposed, [772][256]
+    float* a0t = nullptr;
+    rc = dev_alloc(c, reinterpret_cast<void**>(&a0t), (size_t)256 * (D + 4) * 4, c->allocs);
+    if (rc) return rc;
+    CK(launch_transpose_f32(a0t, a0w, 256, D + 4, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    c->tail = TailWeights{s0w, s0b, s1w, s1b, s3w, s3b, a0t, a0b, a2w, a2b};
 
     std::vector<float2> rt;
     rope_table(rt);
@@ -835,14 +846,25 @@ int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, f
     rc = build_maps(c, (int)bt->n_tokens, &am);
     if (rc) return rc;
     ProfileHook hook;
-    hook.s = s;
-    for (int it = 0; it < iters; it++) {
-        for (int i = 0; i < LAYA_N_STAGES; i++) hook.launches[i] = 0;
-        cudaError_t e = run_forward(c, b, o, am, s, hook);
-        if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile forward: %s", cudaGetErrorString(e));
-        CK(cudaStreamSynchronize(s));
-        hook.collect(stage_ms);
+    hook.s = c->stream;
+    CK(hook.reserve(512));
+    cudaGraph_t graph;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = run_forward(c, b, o, am, c->stream, hook);
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile capture: %s", cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile capture: %s", cudaGetErrorString(e2));
+    cudaGraphExec_t exec;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile instantiate: %s", cudaGetErrorString(e));
+    for (int it = 0; it < iters && e == cudaSuccess; it++) {
+        e = cudaGraphLaunch(exec, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e == cudaSuccess) hook.collect(stage_ms);
     }
+    cudaGraphExecDestroy(exec);
+    if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile run: %s", cudaGetErrorString(e));
     if (stage_launches)
         for (int i = 0; i < LAYA_N_STAGES; i++) stage_launches[i] = hook.launches[i];
     CK(cudaMemcpy(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost));

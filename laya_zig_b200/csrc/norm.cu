@@ -93,13 +93,14 @@ __device__ __forceinline__ void layer_norm(Row& r, const float* w, const float* 
     const float rs = 1.0f / sqrtf(warp_sum(q) * (1.0f / D) + LN_EPS);
 #pragma unroll
     for (int i = 0; i < 3; i++) {
+        // plain loads: w and b may point to global or to shared memory
         const float4* wp = reinterpret_cast<const float4*>(w + i * 256 + lane * 8);
-        const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+        const float4 w0 = wp[0], w1 = wp[1];
         const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         float bb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         if (b) {
             const float4* bp = reinterpret_cast<const float4*>(b + i * 256 + lane * 8);
-            const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+            const float4 b0 = bp[0], b1 = bp[1];
             bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
             bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
         }
@@ -145,17 +146,32 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* __rest
     store16_row<T>(xn + (size_t)t * D, r, lane);
 }
 
-// normIntoJob (src/main.zig:2596-2603): xn = LN(x), x untouched.
+// normIntoJob (src/main.zig:2596-2603): xn = LN(x), x untouched. Each warp
+// takes LN_ROWS rows and issues all their loads first; the block stages the
+// gain and bias in shared memory meanwhile, so a warp waits on memory once.
+constexpr int LN_ROWS = 2;
 template <typename T>
-__global__ void ln_kernel(const float* __restrict__ x, T* __restrict__ xn, const float* __restrict__ w,
-                          const float* __restrict__ b, int M) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(256) ln_kernel(const float* __restrict__ x, T* __restrict__ xn,
+                                                 const float* __restrict__ w, const float* __restrict__ b, int M) {
+    __shared__ __align__(16) float sw[D];
+    __shared__ __align__(16) float sb[D];
+    const int t0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * LN_ROWS;
     const int lane = threadIdx.x & 31;
-    if (t >= M) return;
-    Row r;
-    load_f32_row(r, x + (size_t)t * D, lane);
-    layer_norm(r, w, b, lane);
-    store16_row<T>(xn + (size_t)t * D, r, lane);
+    Row r[LN_ROWS];
+#pragma unroll
+    for (int k = 0; k < LN_ROWS; k++)
+        if (t0 + k < M) load_f32_row(r[k], x + (size_t)(t0 + k) * D, lane);
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        sw[i] = w[i];
+        sb[i] = b ? b[i] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < LN_ROWS; k++) {
+        if (t0 + k >= M) break;
+        layer_norm(r[k], sw, sb, lane);
+        store16_row<T>(xn + (size_t)(t0 + k) * D, r[k], lane);
+    }
 }
 
 // final LN + typeEmbJob (src/main.zig:2708-2711) fused with the first head
@@ -203,7 +219,8 @@ cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_se
 
 cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
+    const int rows_per_block = ROWS_PER_BLOCK * LN_ROWS;  // 8 warps x LN_ROWS rows
+    const int grid = (M + rows_per_block - 1) / rows_per_block;
     if (bf16)
         ln_kernel<__nv_bfloat16><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(x, static_cast<__nv_bfloat16*>(xn), w, b, M);
     else

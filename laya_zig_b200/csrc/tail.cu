@@ -67,61 +67,83 @@ __global__ void marker_ln_kernel(const float* __restrict__ x, const int* __restr
     }
 }
 
-// CTA: 16 markers x 64 scorer outputs; 256 threads, each 1 marker x 4 outputs.
-constexpr int SM_ROWS = 16, SM_COLS = 64, SM_K = 64;
+// scorer.1 + gelu + dot with scorer.3, as an f32 tile GEMM: a CTA takes 32
+// markers x 64 scorer outputs, each of its 256 threads 2 markers x 4 outputs;
+// k-chunks of 32 are staged in shared memory and the next chunk's loads are
+// issued before the current chunk's FMAs. The CTA's 64 outputs of a marker
+// are summed (after gelu and the scorer.3 weights) into one partial sum.
+constexpr int SC_M = 32, SC_N = 64, SC_K = 32;
 __global__ void __launch_bounds__(256) scorer_kernel(const float* __restrict__ mv, int G, const float* __restrict__ w1,
                                                      const float* __restrict__ b1, const float* __restrict__ w3,
                                                      float* __restrict__ partial) {
-    __shared__ float As[SM_ROWS][SM_K + 1];
-    __shared__ float Bs[SM_COLS][SM_K + 1];
-    const int g0 = blockIdx.x * SM_ROWS, j0 = blockIdx.y * SM_COLS;
-    const int tid = threadIdx.x, mr = tid >> 4, jc = (tid & 15) * 4;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k0 = 0; k0 < D; k0 += SM_K) {
-#pragma unroll
-        for (int i = 0; i < (SM_ROWS * SM_K) / 256; i++) {
-            const int e = tid + i * 256, r = e / SM_K, c = e % SM_K;
-            As[r][c] = (g0 + r < G) ? mv[(size_t)(g0 + r) * D + k0 + c] : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < (SM_COLS * SM_K) / 256; i++) {
-            const int e = tid + i * 256, r = e / SM_K, c = e % SM_K;
-            Bs[r][c] = w1[(size_t)(j0 + r) * D + k0 + c];
-        }
+    __shared__ float As[SC_K][SC_M + 4];  // [k][marker]
+    __shared__ float Bs[SC_K][SC_N + 4];  // [k][output]
+    const int g0 = blockIdx.x * SC_M, j0 = blockIdx.y * SC_N;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;  // outputs tx*4.., markers ty*2..
+    // loads: A 32x32 -> 4 floats per thread, B 64x32 -> 8 floats per thread
+    const int ar = tid >> 3, ac = (tid & 7) * 4;        // A row (marker) 0..31, k offset
+    const int br = tid >> 2, bc = (tid & 3) * 8;        // B row (output) 0..63, k offset
+    const bool a_ok = g0 + ar < G;
+    const float* ap = mv + (size_t)(a_ok ? g0 + ar : 0) * D + ac;
+    const float* bp = w1 + (size_t)(j0 + br) * D + bc;
+    float4 ra = a_ok ? *reinterpret_cast<const float4*>(ap) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 rb0 = *reinterpret_cast<const float4*>(bp), rb1 = *reinterpret_cast<const float4*>(bp + 4);
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int k0 = 0; k0 < D; k0 += SC_K) {
         __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < SM_K; k++) {
-            const float a = As[mr][k];
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[i] = fmaf(a, Bs[jc + i][k], acc[i]);
-        }
+        As[ac + 0][ar] = ra.x; As[ac + 1][ar] = ra.y; As[ac + 2][ar] = ra.z; As[ac + 3][ar] = ra.w;
+        Bs[bc + 0][br] = rb0.x; Bs[bc + 1][br] = rb0.y; Bs[bc + 2][br] = rb0.z; Bs[bc + 3][br] = rb0.w;
+        Bs[bc + 4][br] = rb1.x; Bs[bc + 5][br] = rb1.y; Bs[bc + 6][br] = rb1.z; Bs[bc + 7][br] = rb1.w;
         __syncthreads();
-    }
-    float p = 0.f;
+        if (k0 + SC_K < D) {  // next chunk in flight while this one is consumed
+            ra = a_ok ? *reinterpret_cast<const float4*>(ap + k0 + SC_K) : make_float4(0.f, 0.f, 0.f, 0.f);
+            rb0 = *reinterpret_cast<const float4*>(bp + k0 + SC_K);
+            rb1 = *reinterpret_cast<const float4*>(bp + k0 + SC_K + 4);
+        }
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int j = j0 + jc + i;
-        p += gelu_scalar(acc[i] + b1[j]) * w3[j];
+        for (int k = 0; k < SC_K; k++) {
+            const float2 av = *reinterpret_cast<const float2*>(&As[k][ty * 2]);
+            const float4 bv = *reinterpret_cast<const float4*>(&Bs[k][tx * 4]);
+            acc[0][0] = fmaf(av.x, bv.x, acc[0][0]); acc[0][1] = fmaf(av.x, bv.y, acc[0][1]);
+            acc[0][2] = fmaf(av.x, bv.z, acc[0][2]); acc[0][3] = fmaf(av.x, bv.w, acc[0][3]);
+            acc[1][0] = fmaf(av.y, bv.x, acc[1][0]); acc[1][1] = fmaf(av.y, bv.y, acc[1][1]);
+            acc[1][2] = fmaf(av.y, bv.z, acc[1][2]); acc[1][3] = fmaf(av.y, bv.w, acc[1][3]);
+        }
     }
-    // the 16 threads of one marker are lanes 0-15 or 16-31 of a warp
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-    if ((tid & 15) == 0 && g0 + mr < G) partial[(size_t)(g0 + mr) * SCORER_GROUPS + blockIdx.y] = p;
+    for (int i = 0; i < 2; i++) {
+        float p = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int j = j0 + tx * 4 + c;
+            p += gelu_scalar(acc[i][c] + b1[j]) * w3[j];
+        }
+        // the 16 threads sharing a marker are 16 consecutive lanes
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+        const int g = g0 + ty * 2 + i;
+        if (tx == 0 && g < G) partial[(size_t)g * SCORER_GROUPS + blockIdx.y] = p;
+    }
 }
 
-// one CTA (256 threads) per sequence
-__global__ void __launch_bounds__(256) act_kernel(const float* __restrict__ x, const int* __restrict__ cu_seqlens,
-                                                  const int* __restrict__ cu_markers,
-                                                  const float* __restrict__ partial, TailWeights w,
-                                                  float* __restrict__ logits, float* __restrict__ act,
-                                                  float* __restrict__ pooled) {
+// One CTA (1024 threads) per sequence: logits from the partial sums, pooled
+// = x[CLS], the act features, then [pooled | features] (772) -> 256 with the
+// transposed act_head.0 weight (thread j of each 256-thread slice reads
+// column j: coalesced), gelu, -> 2, softmax.
+constexpr int ACT_THREADS = 1024, ACT_SLICES = ACT_THREADS / 256, ACT_IN = D + 4;
+__global__ void __launch_bounds__(ACT_THREADS) act_kernel(const float* __restrict__ x,
+                                                          const int* __restrict__ cu_seqlens,
+                                                          const int* __restrict__ cu_markers,
+                                                          const float* __restrict__ partial, TailWeights w,
+                                                          float* __restrict__ logits, float* __restrict__ act,
+                                                          float* __restrict__ pooled) {
     __shared__ float lg[MAX_MARKERS_PER_SEQ];
-    __shared__ float act_in[D + 4];
-    __shared__ float h256[256];
+    __shared__ float act_in[ACT_IN];
+    __shared__ float hpart[ACT_SLICES][256];
     __shared__ float a2[2];
     const int s = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gb = cu_markers[s], K = min(cu_markers[s + 1] - gb, MAX_MARKERS_PER_SEQ);
-    for (int r = tid; r < K; r += 256) {
+    for (int r = tid; r < K; r += ACT_THREADS) {
         float v = 0.f;
         for (int c = 0; c < SCORER_GROUPS; c++) v += partial[(size_t)(gb + r) * SCORER_GROUPS + c];
         v += w.s3b[0];
@@ -129,7 +151,7 @@ __global__ void __launch_bounds__(256) act_kernel(const float* __restrict__ x, c
         logits[gb + r] = v;
     }
     const float* cls = x + (size_t)cu_seqlens[s] * D;
-    for (int c = tid; c < D; c += 256) {
+    for (int c = tid; c < D; c += ACT_THREADS) {
         act_in[c] = cls[c];
         pooled[(size_t)s * D + c] = cls[c];
     }
@@ -165,17 +187,31 @@ __global__ void __launch_bounds__(256) act_kernel(const float* __restrict__ x, c
         act_in[D + 3] = kk / 255.0f;
     }
     __syncthreads();
-    for (int i = warp; i < 256; i += 8) {
-        const float* wr = w.a0w + (size_t)i * (D + 4);
-        float p = 0.f;
-        for (int k = lane; k < D + 4; k += 32) p = fmaf(act_in[k], wr[k], p);
-        p = warp_sum(p);
-        if (lane == 0) h256[i] = gelu_scalar(p + w.a0b[i]);
+    {
+        const int j = tid & 255, sl = tid >> 8;
+        const int k0 = sl * ((ACT_IN + ACT_SLICES - 1) / ACT_SLICES);
+        const int k1 = min(ACT_IN, k0 + (ACT_IN + ACT_SLICES - 1) / ACT_SLICES);
+        float p0 = 0.f, p1 = 0.f;
+        int k = k0;
+#pragma unroll 4
+        for (; k + 1 < k1; k += 2) {
+            p0 = fmaf(act_in[k], w.a0t[(size_t)k * 256 + j], p0);
+            p1 = fmaf(act_in[k + 1], w.a0t[(size_t)(k + 1) * 256 + j], p1);
+        }
+        if (k < k1) p0 = fmaf(act_in[k], w.a0t[(size_t)k * 256 + j], p0);
+        hpart[sl][j] = p0 + p1;
+    }
+    __syncthreads();
+    if (tid < 256) {
+        float h = 0.f;
+#pragma unroll
+        for (int sl = 0; sl < ACT_SLICES; sl++) h += hpart[sl][tid];
+        hpart[0][tid] = gelu_scalar(h + w.a0b[tid]);
     }
     __syncthreads();
     if (warp < 2) {
         float p = 0.f;
-        for (int k = lane; k < 256; k += 32) p = fmaf(h256[k], w.a2w[warp * 256 + k], p);
+        for (int k = lane; k < 256; k += 32) p = fmaf(hpart[0][k], w.a2w[warp * 256 + k], p);
         p = warp_sum(p);
         if (lane == 0) a2[warp] = p + w.a2b[warp];
     }
@@ -199,10 +235,9 @@ cudaError_t launch_tail(const float* x, const int* cu_seqlens, const uint32_t* m
     if (G > 0) {
         marker_ln_kernel<<<(G + 7) / 8, 256, 0, s>>>(x, cu_seqlens, markers, cu_markers, n_seqs, G, w.s0w, w.s0b, mv,
                                                      err);
-        scorer_kernel<<<dim3((G + SM_ROWS - 1) / SM_ROWS, D / SM_COLS), 256, 0, s>>>(mv, G, w.s1w, w.s1b, w.s3w,
-                                                                                      partial);
+        scorer_kernel<<<dim3((G + SC_M - 1) / SC_M, D / SC_N), 256, 0, s>>>(mv, G, w.s1w, w.s1b, w.s3w, partial);
     }
-    act_kernel<<<n_seqs, 256, 0, s>>>(x, cu_seqlens, cu_markers, partial, w, logits, act, pooled);
+    act_kernel<<<n_seqs, ACT_THREADS, 0, s>>>(x, cu_seqlens, cu_markers, partial, w, logits, act, pooled);
     return cudaGetLastError();
 }
 
