@@ -109,11 +109,13 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
     __shared__ __align__(128) T sK[2][KB * 64];
     __shared__ __align__(128) T sV[2][KB * 64];
 
+    griddep_launch();
     const int seq = blockIdx.z, h = blockIdx.y;
-    const int start = cu_seqlens[seq];
+    const int start = cu_seqlens[seq];  // batch offsets: written before the forward starts
     const int L = cu_seqlens[seq + 1] - start;
     const int q0 = blockIdx.x * QB;
     if (q0 >= L) return;
+    griddep_wait();  // qkv comes from the preceding projection
     const int ld = 3 * D;
     const T* base = qkv + (size_t)start * ld;
 
@@ -265,12 +267,10 @@ cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* c
     if (n_seqs <= 0 || max_len <= 0) return cudaSuccess;
     dim3 grid((max_len + QB - 1) / QB, H, n_seqs);
     if (bf16)
-        attention_kernel<__nv_bfloat16><<<grid, THREADS, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, window);
-    else
-        attention_kernel<__half><<<grid, THREADS, 0, stream>>>(static_cast<const __half*>(qkv),
-                                                               static_cast<__half*>(out), cu_seqlens, window);
-    return cudaGetLastError();
+        return launch_k(attention_kernel<__nv_bfloat16>, grid, THREADS, 0, stream,
+                        static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, window);
+    return launch_k(attention_kernel<__half>, grid, THREADS, 0, stream, static_cast<const __half*>(qkv),
+                    static_cast<__half*>(out), cu_seqlens, window);
 }
 
 }  // namespace laya

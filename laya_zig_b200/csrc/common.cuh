@@ -9,6 +9,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <utility>
+
 namespace laya {
 
 constexpr int D = 768;           // hidden size
@@ -256,6 +259,46 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t mask) {
         "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
         ::"r"(smem_u32(bar)), "h"(mask)
         : "memory");
+}
+
+// ------------------------------------------------------------------ dependent launch
+// Every forward kernel is launched with programmatic stream serialisation:
+// it may start while its predecessor in the stream is still finishing, runs
+// only its prologue (shared memory, barriers, TMEM, constant weights), and
+// calls griddep_wait() before touching anything an earlier kernel wrote or
+// will read. griddep_wait() returns once the predecessor has completed and
+// its writes are visible; since that predecessor waited the same way, every
+// earlier kernel has completed too. Launched without the attribute, both
+// calls are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel in the stream start launching (its CTAs still wait in
+// griddep_wait until this grid completes).
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: launch with programmatic stream serialisation (set LAYA_PDL=0 in the
+// environment to launch plainly).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("LAYA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ------------------------------------------------------------------ math

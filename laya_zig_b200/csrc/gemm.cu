@@ -290,6 +290,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Set-up above overlaps the previous kernel's tail; operands and outputs
+    // are touched only after it has completed.
+    griddep_launch();
+    griddep_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -470,15 +474,15 @@ cudaError_t launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const
         const int tiles = ((args.M + 2 * BM - 1) / (2 * BM)) * (args.N / BN);
         const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
         if (pairs <= 0) return cudaSuccess;
-        gemm_pair_kernel<EPI, T><<<2 * pairs, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, out_map, args);
+        return launch_k(gemm_pair_kernel<EPI, T>, 2 * pairs, NUM_THREADS, C::SMEM, stream, a_map, b_map, out_map,
+                        args);
     } else {
         using C = Cfg<BN>;
         const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
         const int grid = tiles < num_sms ? tiles : num_sms;
         if (grid <= 0) return cudaSuccess;
-        gemm_kernel<BN, EPI, T><<<grid, NUM_THREADS, C::SMEM, stream>>>(a_map, b_map, out_map, args);
+        return launch_k(gemm_kernel<BN, EPI, T>, grid, NUM_THREADS, C::SMEM, stream, a_map, b_map, out_map, args);
     }
-    return cudaGetLastError();
 }
 
 template <int BN, typename T>

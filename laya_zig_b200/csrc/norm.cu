@@ -126,6 +126,8 @@ template <typename T>
 __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, int n_seqs, int M,
                              const T* __restrict__ emb, const float* __restrict__ w, float* __restrict__ x,
                              T* __restrict__ xn, int* __restrict__ pos, int* __restrict__ seq_of, int* err) {
+    griddep_wait();
+    griddep_launch();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (t >= M) return;
@@ -155,16 +157,18 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* __restrict__ x, T*
                                                  const float* __restrict__ w, const float* __restrict__ b, int M) {
     __shared__ __align__(16) float sw[D];
     __shared__ __align__(16) float sb[D];
+    griddep_launch();
     const int t0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * LN_ROWS;
     const int lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {  // weights: no earlier kernel writes them
+        sw[i] = w[i];
+        sb[i] = b ? b[i] : 0.0f;
+    }
+    griddep_wait();
     Row r[LN_ROWS];
 #pragma unroll
     for (int k = 0; k < LN_ROWS; k++)
         if (t0 + k < M) load_f32_row(r[k], x + (size_t)(t0 + k) * D, lane);
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        sw[i] = w[i];
-        sb[i] = b ? b[i] : 0.0f;
-    }
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < LN_ROWS; k++) {
@@ -182,6 +186,8 @@ __global__ void final_kernel(float* __restrict__ x, T* __restrict__ xn, const fl
                              const float* __restrict__ type_emb, const uint32_t* __restrict__ qtypes,
                              const int* __restrict__ seq_of, const float* __restrict__ w1,
                              const float* __restrict__ b1, int M) {
+    griddep_wait();
+    griddep_launch();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (t >= M) return;
@@ -207,13 +213,12 @@ cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_se
     if (M <= 0) return cudaSuccess;
     const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
     if (bf16)
-        embed_kernel<__nv_bfloat16><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(
-            ids, cu, n_seqs, M, static_cast<const __nv_bfloat16*>(emb), w, x, static_cast<__nv_bfloat16*>(xn), pos,
-            seq_of, err);
+        return launch_k(embed_kernel<__nv_bfloat16>, grid, 32 * ROWS_PER_BLOCK, 0, s, ids, cu, n_seqs, M,
+                        static_cast<const __nv_bfloat16*>(emb), w, x, static_cast<__nv_bfloat16*>(xn), pos, seq_of,
+                        err);
     else
-        embed_kernel<__half><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(ids, cu, n_seqs, M,
-                                                                   static_cast<const __half*>(emb), w, x,
-                                                                   static_cast<__half*>(xn), pos, seq_of, err);
+        return launch_k(embed_kernel<__half>, grid, 32 * ROWS_PER_BLOCK, 0, s, ids, cu, n_seqs, M,
+                        static_cast<const __half*>(emb), w, x, static_cast<__half*>(xn), pos, seq_of, err);
     return cudaGetLastError();
 }
 
@@ -222,9 +227,10 @@ cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const
     const int rows_per_block = ROWS_PER_BLOCK * LN_ROWS;  // 8 warps x LN_ROWS rows
     const int grid = (M + rows_per_block - 1) / rows_per_block;
     if (bf16)
-        ln_kernel<__nv_bfloat16><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(x, static_cast<__nv_bfloat16*>(xn), w, b, M);
+        return launch_k(ln_kernel<__nv_bfloat16>, grid, 32 * ROWS_PER_BLOCK, 0, s, x,
+                        static_cast<__nv_bfloat16*>(xn), w, b, M);
     else
-        ln_kernel<__half><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(x, static_cast<__half*>(xn), w, b, M);
+        return launch_k(ln_kernel<__half>, grid, 32 * ROWS_PER_BLOCK, 0, s, x, static_cast<__half*>(xn), w, b, M);
     return cudaGetLastError();
 }
 
@@ -234,11 +240,11 @@ cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const f
     if (M <= 0) return cudaSuccess;
     const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
     if (bf16)
-        final_kernel<__nv_bfloat16><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(
-            x, static_cast<__nv_bfloat16*>(xn), wf, type_emb, qtypes, seq_of, w1, b1, M);
+        return launch_k(final_kernel<__nv_bfloat16>, grid, 32 * ROWS_PER_BLOCK, 0, s, x,
+                        static_cast<__nv_bfloat16*>(xn), wf, type_emb, qtypes, seq_of, w1, b1, M);
     else
-        final_kernel<__half><<<grid, 32 * ROWS_PER_BLOCK, 0, s>>>(x, static_cast<__half*>(xn), wf, type_emb,
-                                                                   qtypes, seq_of, w1, b1, M);
+        return launch_k(final_kernel<__half>, grid, 32 * ROWS_PER_BLOCK, 0, s, x, static_cast<__half*>(xn), wf,
+                        type_emb, qtypes, seq_of, w1, b1, M);
     return cudaGetLastError();
 }
 

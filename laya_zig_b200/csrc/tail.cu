@@ -38,6 +38,8 @@ __global__ void marker_ln_kernel(const float* __restrict__ x, const int* __restr
                                  const uint32_t* __restrict__ markers, const int* __restrict__ cu_markers, int n_seqs,
                                  int G, const float* __restrict__ w, const float* __restrict__ b,
                                  float* __restrict__ mv, int* err) {
+    griddep_wait();
+    griddep_launch();
     const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (g >= G) return;
@@ -86,8 +88,10 @@ __global__ void __launch_bounds__(256) scorer_kernel(const float* __restrict__ m
     const bool a_ok = g0 + ar < G;
     const float* ap = mv + (size_t)(a_ok ? g0 + ar : 0) * D + ac;
     const float* bp = w1 + (size_t)(j0 + br) * D + bc;
+    griddep_launch();
+    float4 rb0 = *reinterpret_cast<const float4*>(bp), rb1 = *reinterpret_cast<const float4*>(bp + 4);  // weights
+    griddep_wait();  // mv comes from the marker LayerNorm
     float4 ra = a_ok ? *reinterpret_cast<const float4*>(ap) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 rb0 = *reinterpret_cast<const float4*>(bp), rb1 = *reinterpret_cast<const float4*>(bp + 4);
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     for (int k0 = 0; k0 < D; k0 += SC_K) {
         __syncthreads();
@@ -141,6 +145,8 @@ __global__ void __launch_bounds__(ACT_THREADS) act_kernel(const float* __restric
     __shared__ float act_in[ACT_IN];
     __shared__ float hpart[ACT_SLICES][256];
     __shared__ float a2[2];
+    griddep_wait();
+    griddep_launch();
     const int s = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gb = cu_markers[s], K = min(cu_markers[s + 1] - gb, MAX_MARKERS_PER_SEQ);
     for (int r = tid; r < K; r += ACT_THREADS) {
@@ -233,12 +239,15 @@ cudaError_t launch_tail(const float* x, const int* cu_seqlens, const uint32_t* m
                         float* pooled, int* err, cudaStream_t s) {
     if (n_seqs <= 0) return cudaSuccess;
     if (G > 0) {
-        marker_ln_kernel<<<(G + 7) / 8, 256, 0, s>>>(x, cu_seqlens, markers, cu_markers, n_seqs, G, w.s0w, w.s0b, mv,
-                                                     err);
-        scorer_kernel<<<dim3((G + SC_M - 1) / SC_M, D / SC_N), 256, 0, s>>>(mv, G, w.s1w, w.s1b, w.s3w, partial);
+        cudaError_t e = launch_k(marker_ln_kernel, (G + 7) / 8, 256, 0, s, x, cu_seqlens, markers, cu_markers, n_seqs,
+                                 G, w.s0w, w.s0b, mv, err);
+        if (e != cudaSuccess) return e;
+        e = launch_k(scorer_kernel, dim3((G + SC_M - 1) / SC_M, D / SC_N), 256, 0, s, mv, G, w.s1w, w.s1b, w.s3w,
+                     partial);
+        if (e != cudaSuccess) return e;
     }
-    act_kernel<<<n_seqs, ACT_THREADS, 0, s>>>(x, cu_seqlens, cu_markers, partial, w, logits, act, pooled);
-    return cudaGetLastError();
+    return launch_k(act_kernel, n_seqs, ACT_THREADS, 0, s, x, cu_seqlens, cu_markers, partial, w, logits, act,
+                    pooled);
 }
 
 }  // namespace laya
