@@ -7,8 +7,10 @@
 // warps hold 16 rows each. Scores and P.V run on the tensor cores
 // (mma.sync m16n8k16, f32 accumulate); the softmax is the online
 // (running max / running sum) form in f32 with exp2, normalised once at the
-// end as the reference does (2479-2486). Key/value tiles of 64 keys are
-// double-buffered in swizzled shared memory with cp.async.
+// end as the reference does (2479-2486). Key/value tiles of 64 keys stream
+// through a 3-deep ring in swizzled shared memory with cp.async; the
+// prologue requests Q and the first three tiles at once, which is every tile
+// a 64-row block of a sequence of up to 192 tokens needs.
 //
 // Inputs come straight from the QKV projection's output: row r of `qkv`
 // holds q | k | v (each 12 heads x 64, RoPE already applied to q and k),
@@ -20,7 +22,9 @@ namespace {
 
 constexpr int QB = 64;   // query rows per CTA
 constexpr int KB = 64;   // keys per tile
+constexpr int NST = 3;   // key/value tiles in flight
 constexpr int THREADS = 128;
+constexpr int SMEM_BYTES = (QB + 2 * NST * KB) * 64 * 2;  // 56 KB
 
 // element offset of (row, col) in a 64x64 16-bit tile whose 16-byte chunks
 // are XOR-swizzled by row, so ldmatrix row fetches never share a bank.
@@ -105,9 +109,10 @@ __device__ __forceinline__ void load_tile(T* tile, const T* src, int ld, int r0,
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
                                                             const int* __restrict__ cu_seqlens, int window) {
-    __shared__ __align__(128) T sQ[QB * 64];
-    __shared__ __align__(128) T sK[2][KB * 64];
-    __shared__ __align__(128) T sV[2][KB * 64];
+    extern __shared__ __align__(128) uint8_t att_smem[];  // Q tile, then NST K tiles, then NST V tiles
+    T* sQ = reinterpret_cast<T*>(att_smem);
+    T* sK = sQ + QB * 64;
+    T* sV = sK + NST * KB * 64;
 
     griddep_launch();
     const int seq = blockIdx.z, h = blockIdx.y;
@@ -127,10 +132,18 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
     const int kt0 = klo / KB, kt1 = (khi + KB - 1) / KB;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Prologue: Q and the first NST key/value tiles all requested at once
+    // (a 64-row block of a <= 192-token sequence needs at most 3), one
+    // commit group per tile so each can be waited for on its own.
     load_tile(sQ, base, ld, q0, L, h * HD);
-    load_tile(sK[0], base, ld, kt0 * KB, L, D + h * HD);
-    load_tile(sV[0], base, ld, kt0 * KB, L, 2 * D + h * HD);
-    cp_commit();
+#pragma unroll
+    for (int i = 0; i < NST; i++) {
+        if (kt0 + i < kt1) {
+            load_tile(sK + i * KB * 64, base, ld, (kt0 + i) * KB, L, D + h * HD);
+            load_tile(sV + i * KB * 64, base, ld, (kt0 + i) * KB, L, 2 * D + h * HD);
+        }
+        cp_commit();
+    }
 
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
     const int qi0 = q0 + warp * 16 + (lane >> 2), qi1 = qi0 + 8;
@@ -141,13 +154,9 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
     uint32_t qa[4][4];
 
     for (int kt = kt0; kt < kt1; kt++) {
-        const int buf = (kt - kt0) & 1;
-        if (kt + 1 < kt1) {
-            load_tile(sK[buf ^ 1], base, ld, (kt + 1) * KB, L, D + h * HD);
-            load_tile(sV[buf ^ 1], base, ld, (kt + 1) * KB, L, 2 * D + h * HD);
-        }
-        cp_commit();
-        cp_wait<1>();
+        const int slot = (kt - kt0) % NST;
+        // NST + (kt - kt0) groups are committed; tile kt's is the oldest pending
+        cp_wait<NST - 1>();
         __syncthreads();
         if (kt == kt0) {
 #pragma unroll
@@ -160,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
         float s[8][4];
 #pragma unroll
         for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-        const T* K = sK[buf];
+        const T* K = sK + slot * KB * 64;
 #pragma unroll
         for (int ks = 0; ks < 4; ks++) {
 #pragma unroll
@@ -227,7 +236,7 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
             o[j][3] *= a1;
         }
         // O += P V: P as the A operand straight from the score registers
-        const T* V = sV[buf];
+        const T* V = sV + slot * KB * 64;
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
             uint32_t pa[4];
@@ -244,7 +253,12 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
                 mma16816<T>(o[2 * dp + 1], pa, b[2], b[3]);
             }
         }
-        __syncthreads();
+        __syncthreads();  // every warp is done with this slot before it is refilled
+        if (kt + NST < kt1) {
+            load_tile(sK + slot * KB * 64, base, ld, (kt + NST) * KB, L, D + h * HD);
+            load_tile(sV + slot * KB * 64, base, ld, (kt + NST) * KB, L, 2 * D + h * HD);
+        }
+        cp_commit();  // possibly empty: keeps one group per tile
     }
 
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -267,10 +281,18 @@ cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* c
     if (n_seqs <= 0 || max_len <= 0) return cudaSuccess;
     dim3 grid((max_len + QB - 1) / QB, H, n_seqs);
     if (bf16)
-        return launch_k(attention_kernel<__nv_bfloat16>, grid, THREADS, 0, stream,
+        return launch_k(attention_kernel<__nv_bfloat16>, grid, THREADS, SMEM_BYTES, stream,
                         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, window);
-    return launch_k(attention_kernel<__half>, grid, THREADS, 0, stream, static_cast<const __half*>(qkv),
+    return launch_k(attention_kernel<__half>, grid, THREADS, SMEM_BYTES, stream, static_cast<const __half*>(qkv),
                     static_cast<__half*>(out), cu_seqlens, window);
+}
+
+cudaError_t attention_prepare() {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attention_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    return e;
 }
 
 }  // namespace laya

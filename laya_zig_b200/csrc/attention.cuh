@@ -10,4 +10,8 @@ namespace laya {
 cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* cu_seqlens, int n_seqs, int max_len,
                              int window, cudaStream_t stream);
 
+// Raise the attention kernels' dynamic shared-memory limit on the current
+// device (before any capture).
+cudaError_t attention_prepare();
+
 }  // namespace laya

@@ -645,6 +645,7 @@ int create_impl(laya_ctx* c, const laya_tensor* t, int n) {
     CK(cudaMemcpyAsync(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     CK(gemm_prepare());
+    CK(attention_prepare());
     return LAYA_OK;
 }
 
