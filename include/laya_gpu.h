@@ -173,11 +173,13 @@ typedef enum {
     LAYA_N_STAGES = 9
 } laya_stage;
 
-/* --profile: run `iters` forwards of a device batch eagerly (no graph) with
- * a CUDA event pair around every kernel on `stream` (a cudaStream_t, NULL =
- * the legacy default stream). stage_ms[LAYA_N_STAGES] receives the summed kernel time per
- * stage over all iterations, stage_launches[LAYA_N_STAGES] the launches per
- * forward. Synchronous. */
+/* --profile: capture one forward of a device batch as a CUDA graph with an
+ * external event record node on either side of every kernel, then launch it
+ * `iters` times on `stream` (a cudaStream_t, NULL = the legacy default
+ * stream), so the kernels run back to back as in the timed path.
+ * stage_ms[LAYA_N_STAGES] receives the summed kernel time per stage over all
+ * iterations, stage_launches[LAYA_N_STAGES] the launches per forward.
+ * Synchronous. */
 LAYA_API int laya_gpu_forward_profile(laya_ctx* ctx, const laya_batch* batch, float* logits, float* act, int iters,
                                       void* stream, float* stage_ms, int* stage_launches);
 
