@@ -7,7 +7,8 @@ namespace laya {
 // norm.cu ------------------------------------------------------------------
 cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_seqs, int M, const void* emb,
                          const float* w, float* x, void* xn, int* pos, int* seq_of, int* err, cudaStream_t s);
-cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, cudaStream_t s);
+cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, int num_sms,
+                      cudaStream_t s);
 cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const float* type_emb,
                          const uint32_t* qtypes, const int* seq_of, const float* w1, const float* b1, int M,
                          cudaStream_t s);

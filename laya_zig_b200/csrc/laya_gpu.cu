@@ -292,13 +292,13 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
     hook.tap(0);
     for (int l = 0; l < NL; l++) {
         const EncW& w = c->enc[l];
-        if (w.attn_norm) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.attn_norm, nullptr, M, s));
+        if (w.attn_norm) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.attn_norm, nullptr, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_QKV,
             gemm(c, EPI_QKV, am.a_xn, w.m_qkv, am.o_qkv, M, 3 * D, D, nullptr, 2 * D, s));
         RUN(LAYA_STAGE_ATTN,
             launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, (l % 3) ? WINDOW : -1, s));
         RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_wo, am.o_x, M, D, D, nullptr, 0, s));
-        RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.mlp_norm, nullptr, M, s));
+        RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.mlp_norm, nullptr, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_UP,
             gemm(c, EPI_GLU, am.a_xn, w.m_wi, am.o_mlp, M, 2 * INTER, D, nullptr, 0, s));
         RUN(LAYA_STAGE_GEMM_DOWN, gemm(c, EPI_RESID, am.a_mlp, w.m_wo2, am.o_x, M, D, INTER, nullptr, 0, s));
@@ -309,11 +309,11 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
     hook.tap(24);
     for (int l = 0; l < HEAD_LAYERS; l++) {
         const HeadW& w = c->head[l];
-        if (l > 0) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n1w, w.n1b, M, s));
+        if (l > 0) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n1w, w.n1b, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_QKV, gemm(c, EPI_QKV, am.a_xn, w.m_in, am.o_qkv, M, 3 * D, D, w.in_b, 0, s));
         RUN(LAYA_STAGE_ATTN, launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, -1, s));
         RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_out, am.o_x, M, D, D, w.out_b, 0, s));
-        RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n2w, w.n2b, M, s));
+        RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n2w, w.n2b, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_UP,
             gemm(c, EPI_RELU, am.a_xn, w.m_l1, am.o_ff, M, HEAD_FF, D, w.l1_b, 0, s));
         RUN(LAYA_STAGE_GEMM_DOWN,

@@ -148,33 +148,41 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* __rest
     store16_row<T>(xn + (size_t)t * D, r, lane);
 }
 
-// normIntoJob (src/main.zig:2596-2603): xn = LN(x), x untouched. Each warp
-// takes LN_ROWS rows and issues all their loads first; the block stages the
-// gain and bias in shared memory meanwhile, so a warp waits on memory once.
-constexpr int LN_ROWS = 2;
+// normIntoJob (src/main.zig:2596-2603): xn = LN(x), x untouched. The grid
+// is sized to the SMs' resident blocks and each warp strides over rows,
+// loading its next row while it normalises the current one, so every warp
+// keeps a row's loads in flight; the block stages the gain and bias in
+// shared memory once.
 template <typename T>
 __global__ void __launch_bounds__(256) ln_kernel(const float* __restrict__ x, T* __restrict__ xn,
                                                  const float* __restrict__ w, const float* __restrict__ b, int M) {
     __shared__ __align__(16) float sw[D];
     __shared__ __align__(16) float sb[D];
     griddep_launch();
-    const int t0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * LN_ROWS;
     const int lane = threadIdx.x & 31;
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     for (int i = threadIdx.x; i < D; i += blockDim.x) {  // weights: no earlier kernel writes them
         sw[i] = w[i];
         sb[i] = b ? b[i] : 0.0f;
     }
     griddep_wait();
-    Row r[LN_ROWS];
-#pragma unroll
-    for (int k = 0; k < LN_ROWS; k++)
-        if (t0 + k < M) load_f32_row(r[k], x + (size_t)(t0 + k) * D, lane);
+    Row ra, rb;
+    if (row < M) load_f32_row(ra, x + (size_t)row * D, lane);
     __syncthreads();
-#pragma unroll
-    for (int k = 0; k < LN_ROWS; k++) {
-        if (t0 + k >= M) break;
-        layer_norm(r[k], sw, sb, lane);
-        store16_row<T>(xn + (size_t)(t0 + k) * D, r[k], lane);
+    // two row buffers used in turn: no register copies between iterations
+    while (row < M) {
+        int next = row + nw;
+        if (next < M) load_f32_row(rb, x + (size_t)next * D, lane);
+        layer_norm(ra, sw, sb, lane);
+        store16_row<T>(xn + (size_t)row * D, ra, lane);
+        row = next;
+        if (row >= M) break;
+        next = row + nw;
+        if (next < M) load_f32_row(ra, x + (size_t)next * D, lane);
+        layer_norm(rb, sw, sb, lane);
+        store16_row<T>(xn + (size_t)row * D, rb, lane);
+        row = next;
     }
 }
 
@@ -222,10 +230,20 @@ cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_se
     return cudaGetLastError();
 }
 
-cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, cudaStream_t s) {
+cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, int num_sms,
+                      cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    const int rows_per_block = ROWS_PER_BLOCK * LN_ROWS;  // 8 warps x LN_ROWS rows
-    const int grid = (M + rows_per_block - 1) / rows_per_block;
+    // resident blocks per SM, once per process (every device here is a B200)
+    static const int per_sm = [] {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, ln_kernel<__nv_bfloat16>, 32 * ROWS_PER_BLOCK, 0) !=
+                cudaSuccess ||
+            n < 1)
+            n = 1;
+        return n;
+    }();
+    const int blocks_for_rows = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;  // one row per warp
+    const int grid = blocks_for_rows < num_sms * per_sm ? blocks_for_rows : num_sms * per_sm;
     if (bf16)
         return launch_k(ln_kernel<__nv_bfloat16>, grid, 32 * ROWS_PER_BLOCK, 0, s, x,
                         static_cast<__nv_bfloat16*>(xn), w, b, M);
