@@ -121,6 +121,11 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // all committed stores are complete
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// the shared-memory sources of all but the N most recent committed stores have been read
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -302,19 +307,37 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
 }
 
 // ------------------------------------------------------------------ math
+// 1/x and 2^x on the SFU (rcp.approx / ex2.approx: relative error about
+// 2^-23 and 2^-22), for epilogues whose results are rounded to 16 bits.
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // erf by Abramowitz-Stegun 7.1.26 and gelu in the |x| form the reference's
-// vector path uses (src/main.zig:60-70, 621-630).
+// vector path uses (src/main.zig:60-70, 621-630):
+//   gelu(x) = (x + |x| erf(|x|/sqrt2)) / 2,
+//   erf(a) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-a^2),
+//   t = 1 / (1 + p a),
+// with exp(-a^2) = 2^(-a^2 log2 e) and the reciprocal on the SFU; their
+// ~1e-7 relative errors vanish in the 16-bit rounding of the product.
 __device__ __forceinline__ float gelu_as(float x) {
     const float ax = fabsf(x);
     const float a = ax * 0.7071067811865476f;
-    const float t = 1.0f / (1.0f + a * 0.3275911f);
+    const float t = rcp_approx(fmaf(a, 0.3275911f, 1.0f));
     float p = 1.061405429f;
     p = fmaf(p, t, -1.453152027f);
     p = fmaf(p, t, 1.421413741f);
     p = fmaf(p, t, -0.284496736f);
     p = fmaf(p, t, 0.254829592f);
-    const float e = 1.0f - (p * t) * expf(-a * a);
-    return 0.5f * (x + ax * e);
+    const float e = fmaf(-(p * t), ex2_approx(-1.4426950408889634f * (a * a)), 1.0f);
+    return 0.5f * fmaf(ax, e, x);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

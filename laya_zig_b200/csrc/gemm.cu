@@ -32,18 +32,30 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
-constexpr int STAGING_BYTES = 32 * 128;  // one 32-row x 128-byte output tile per epilogue warp
+constexpr int STAGING_BYTES = 32 * 128;  // one 32-row x 128-byte output tile
+// Staging tiles per epilogue warp: two for the 16-bit epilogues, so one
+// drains to the TMA unit while the next fills; one for the f32 ones, whose
+// TMA reduce-adds are paced by L2 and gain more from a deeper operand ring.
+template <int EPI>
+constexpr int staging_bufs() {
+    return (EPI == EPI_F32 || EPI == EPI_RESID) ? 1 : 2;
+}
+constexpr int SMEM_LIMIT = 227 * 1024;
 
-template <int BN, bool PAIR = false>
+template <int BN, int EPI, bool PAIR = false>
 struct Cfg {
+    static constexpr int STAGING_BUFS = staging_bufs<EPI>();
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B rows this CTA loads per tile
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (STAGE_BYTES >= 48 * 1024) ? 4 : 6;
+    static constexpr int FIXED = EPI_WARPS * STAGING_BUFS * STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
+    static constexpr int STAGES = FIT < 6 ? FIT : 6;
     static constexpr int RING = STAGES * STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // two accumulators of BN f32 columns
-    static constexpr int SMEM = RING + EPI_WARPS * STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int SMEM = RING + FIXED;
+    static_assert(STAGES >= 3, "operand ring too shallow");
 };
 
 template <typename T>
@@ -129,14 +141,23 @@ __device__ __forceinline__ void flush_stage(const CUtensorMap* map, uint8_t* til
     }
 }
 
-// Before rewriting the staging tile: its previous store has read it.
-__device__ __forceinline__ void reuse_stage(int lane) {
-    if (lane == 0) bulk_wait_read_all();
-    __syncwarp();
-}
+// An epilogue warp's NBUF staging tiles, used in turn: the next one to fill
+// is free once the store issued NBUF tiles ago has read it (lane 0 issues
+// and commits every store, so its bulk groups are the warp's).
+template <int NBUF>
+struct Staging {
+    uint8_t* base;
+    int n;  // tiles handed out so far
+    __device__ __forceinline__ uint8_t* next(int lane) {
+        if (lane == 0) bulk_wait_read<NBUF - 1>();
+        __syncwarp();
+        return base + (n++ % NBUF) * STAGING_BYTES;
+    }
+};
 
 template <int BN, int EPI, typename T>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* out_map, uint8_t* tile,
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* out_map,
+                                              Staging<staging_bufs<EPI>()>& st,
                                               uint32_t tacc, int half, int lane, int m0q, int n_blk) {
     constexpr int HALF = BN / 2;  // accumulator columns this warp owns
     if constexpr (EPI == EPI_GLU) {
@@ -144,6 +165,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
         // this warp produces output columns [half*BN/4, (half+1)*BN/4) of the tile
         constexpr int OUT = BN / 4;
         static_assert(OUT == 64 || OUT == 32, "GLU tile");
+        uint8_t* tile = nullptr;
 #pragma unroll 1
         for (int c = 0; c < OUT; c += 32) {
             float g[32], u[32];
@@ -151,7 +173,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
             load_cols(tacc + HALF + half * OUT + c, u);
 #pragma unroll
             for (int i = 0; i < 32; i++) g[i] = gelu_as(g[i]) * u[i];
-            if (c == 0) reuse_stage(lane);
+            if (c == 0) tile = st.next(lane);
             stage16<T>(tile, lane, (c / 32) * 4, g);
         }
         flush_stage<false>(out_map, tile, lane, n_blk * HALF + half * OUT, m0q);
@@ -186,7 +208,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
                     x1[d + 1] = b1 * t.z + a1 * t.w;
                 }
             }
-            reuse_stage(lane);
+            uint8_t* tile = st.next(lane);
             stage16<T>(tile, lane, 0, x0);
             stage16<T>(tile, lane, 4, x1);
             flush_stage<false>(out_map, tile, lane, col, m0q);
@@ -198,7 +220,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
             load_cols(tacc + half * HALF + c, v);
             const int col = n_blk * BN + half * HALF + c;
             add_bias(v, a.bias, col);
-            reuse_stage(lane);
+            uint8_t* tile = st.next(lane);
             stage32(tile, lane, v);
             flush_stage<EPI == EPI_RESID>(out_map, tile, lane, col, m0q);
         }
@@ -218,7 +240,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
                     x1[i] = fmaxf(x1[i], 0.0f);
                 }
             }
-            reuse_stage(lane);
+            uint8_t* tile = st.next(lane);
             stage16<T>(tile, lane, 0, x0);
             stage16<T>(tile, lane, 4, x1);
             flush_stage<false>(out_map, tile, lane, col, m0q);
@@ -232,13 +254,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
 template <int BN, int EPI, typename T, bool PAIR>
 __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtensorMap& b_map,
                                           const CUtensorMap& out_map, const GemmArgs& args) {
-    using C = Cfg<BN, PAIR>;
+    using C = Cfg<BN, EPI, PAIR>;
     constexpr int TILE_M = PAIR ? 2 * BM : BM;
     constexpr uint32_t IDESC = idesc_f16(TILE_M, BN, std::is_same<T, __nv_bfloat16>::value);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + C::RING;
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + EPI_WARPS * STAGING_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + EPI_WARPS * C::STAGING_BUFS * STAGING_BYTES);
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + 2;
@@ -394,7 +416,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
         const int e = warp - 2;
         const int q = warp & 3;          // TMEM lane quarter this warp may access
         const int half = e >> 2;         // which half of the tile's columns
-        uint8_t* tile = staging + e * STAGING_BYTES;
+        Staging<C::STAGING_BUFS> st{staging + e * C::STAGING_BUFS * STAGING_BYTES, 0};
         const uint32_t tempty_leader = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0;
         int it = 0;
         for (int t = unit; t < total; t += units, it++) {
@@ -407,7 +429,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
             tc_fence_after();
             const int m0q = (t / tiles_n) * TILE_M + (int)rank * BM + q * 32;
             const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-            epilogue_tile<BN, EPI, T>(args, &out_map, tile, tacc, half, lane, m0q, t % tiles_n);
+            epilogue_tile<BN, EPI, T>(args, &out_map, st, tacc, half, lane, m0q, t % tiles_n);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -447,10 +469,10 @@ template <int BN, int EPI, typename T>
 cudaError_t prepare_one() {
     if constexpr (BN == 256)
         return cudaFuncSetAttribute(gemm_pair_kernel<EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    Cfg<256, true>::SMEM);
+                                    Cfg<256, EPI, true>::SMEM);
     else
         return cudaFuncSetAttribute(gemm_kernel<BN, EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    Cfg<BN>::SMEM);
+                                    Cfg<BN, EPI>::SMEM);
 }
 
 template <int BN, typename T>
@@ -470,14 +492,14 @@ template <int BN, int EPI, typename T>
 cudaError_t launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const CUtensorMap& out_map,
                        const GemmArgs& args, int num_sms, cudaStream_t stream) {
     if constexpr (BN == 256) {
-        using C = Cfg<256, true>;
+        using C = Cfg<256, EPI, true>;
         const int tiles = ((args.M + 2 * BM - 1) / (2 * BM)) * (args.N / BN);
         const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
         if (pairs <= 0) return cudaSuccess;
         return launch_k(gemm_pair_kernel<EPI, T>, 2 * pairs, NUM_THREADS, C::SMEM, stream, a_map, b_map, out_map,
                         args);
     } else {
-        using C = Cfg<BN>;
+        using C = Cfg<BN, EPI>;
         const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
         const int grid = tiles < num_sms ? tiles : num_sms;
         if (grid <= 0) return cudaSuccess;
