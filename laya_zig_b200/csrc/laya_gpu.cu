@@ -85,13 +85,13 @@ struct laya_ctx {
     void *xn = nullptr, *qkv = nullptr, *ctxb = nullptr, *mlp = nullptr, *ff = nullptr;
     int *pos = nullptr, *seq_of = nullptr;
     float *mv = nullptr, *partial = nullptr;
-    // staged batch inputs / outputs for the host-buffer entry points
-    uint32_t* d_ids = nullptr;
-    int* d_cu = nullptr;
-    uint32_t* d_qt = nullptr;
-    uint32_t* d_mk = nullptr;
-    int* d_cum = nullptr;
-    float *d_logits = nullptr, *d_act = nullptr, *d_pooled = nullptr;
+    // Staged batch inputs / outputs of the host-buffer entry points. d_in
+    // holds ids | cu_seqlens | qtypes | markers | cu_markers packed for the
+    // batch at hand, the same layout as the pinned staging buffer, so one
+    // copy moves them; d_out holds act | logits, read back in one copy.
+    uint32_t* d_in = nullptr;
+    float* d_out = nullptr;
+    float* d_pooled = nullptr;
     int* d_err = nullptr;
     int* h_err = nullptr;  // pinned
     void* h_stage = nullptr;
@@ -175,6 +175,12 @@ int weight_map(laya_ctx* c, CUtensorMap* m, const void* w, uint64_t rows, uint64
     return LAYA_OK;
 }
 
+// Words of the packed batch inputs (ids, cu_seqlens, qtypes, markers,
+// cu_markers) and outputs (act, logits); host outputs start at out_offset.
+size_t in_words(int M, int S, int G) { return (size_t)M + (S + 1) + S + G + (S + 1); }
+size_t out_words(int S, int G) { return (size_t)S * 2 + G; }
+size_t out_offset(const laya_ctx* c) { return (in_words(c->capM, c->capS, c->capG) * 4 + 63) & ~(size_t)63; }
+
 void free_workspace(laya_ctx* c) {
     for (auto& g : c->graphs) cudaGraphExecDestroy(g.second);
     c->graphs.clear();
@@ -201,13 +207,8 @@ int ensure_workspace(laya_ctx* c, int M, int S, int G) {
     A((void**)&c->seq_of, (size_t)nM * 4);
     A((void**)&c->mv, (size_t)nG * D * 4);
     A((void**)&c->partial, (size_t)nG * SCORER_GROUPS * 4);
-    A((void**)&c->d_ids, (size_t)nM * 4);
-    A((void**)&c->d_cu, (size_t)(nS + 1) * 4);
-    A((void**)&c->d_qt, (size_t)nS * 4);
-    A((void**)&c->d_mk, (size_t)nG * 4);
-    A((void**)&c->d_cum, (size_t)(nS + 1) * 4);
-    A((void**)&c->d_logits, (size_t)nG * 4);
-    A((void**)&c->d_act, (size_t)nS * 2 * 4);
+    A((void**)&c->d_in, in_words(nM, nS, nG) * 4);
+    A((void**)&c->d_out, out_words(nS, nG) * 4);
     A((void**)&c->d_pooled, (size_t)nS * D * 4);
     if (rc) {
         free_workspace(c);
@@ -216,8 +217,7 @@ int ensure_workspace(laya_ctx* c, int M, int S, int G) {
     c->capM = nM;
     c->capS = nS;
     c->capG = nG;
-    const size_t stage = (size_t)nM * 4 + (size_t)(nS + 1) * 8 + (size_t)nS * 4 + (size_t)nG * 4 + 64 +
-                         (size_t)nG * 4 + (size_t)nS * 8;
+    const size_t stage = out_offset(c) + out_words(nS, nG) * 4;
     if (stage > c->h_stage_bytes) {
         if (c->h_stage) cudaFreeHost(c->h_stage);
         c->h_stage = nullptr;
@@ -519,12 +519,27 @@ int stage_batch(laya_ctx* c, const laya_seq* seqs, uint32_t n, int M, int G, int
         h_cum[s + 1] = g;
         h_qt[s] = seqs[s].qtype;
     }
-    CK(cudaMemcpyAsync(c->d_ids, h_ids, (size_t)M * 4, cudaMemcpyHostToDevice, c->stream));
-    CK(cudaMemcpyAsync(c->d_cu, h_cu, (size_t)(S + 1) * 4, cudaMemcpyHostToDevice, c->stream));
-    CK(cudaMemcpyAsync(c->d_qt, h_qt, (size_t)S * 4, cudaMemcpyHostToDevice, c->stream));
-    if (G) CK(cudaMemcpyAsync(c->d_mk, h_mk, (size_t)G * 4, cudaMemcpyHostToDevice, c->stream));
-    CK(cudaMemcpyAsync(c->d_cum, h_cum, (size_t)(S + 1) * 4, cudaMemcpyHostToDevice, c->stream));
-    *b = Batch{c->d_ids, c->d_cu, c->d_mk, c->d_cum, c->d_qt, S, M, G, maxlen};
+    CK(cudaMemcpyAsync(c->d_in, h, in_words(M, S, G) * 4, cudaMemcpyHostToDevice, c->stream));
+    uint32_t* d = c->d_in;  // the same offsets on the device
+    *b = Batch{d, reinterpret_cast<const int*>(d + M), d + M + (S + 1) + S,
+               reinterpret_cast<const int*>(d + M + (S + 1) + S + G), d + M + (S + 1), S, M, G, maxlen};
+    return LAYA_OK;
+}
+
+// Device outputs of a staged batch of S sequences and G markers.
+Outs staged_outs(laya_ctx* c, int S, float* pooled, float* hidden) {
+    return Outs{c->d_out + 2 * S, c->d_out, pooled, hidden};
+}
+
+// After the forward: the error word and act | logits into pinned memory,
+// one copy each (optional pooled / hidden straight to the caller).
+int read_back(laya_ctx* c, int S, int G, float* logits, float* act) {
+    float* h_out = reinterpret_cast<float*>(static_cast<uint8_t*>(c->h_stage) + out_offset(c));
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(h_out, c->d_out, out_words(S, G) * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    memcpy(act, h_out, (size_t)S * 8);
+    if (G) memcpy(logits, h_out + 2 * S, (size_t)G * 4);
     return LAYA_OK;
 }
 
@@ -724,15 +739,13 @@ int laya_gpu_forward_batch(laya_ctx* c, const laya_seq* seqs, uint32_t n, float*
     if (rc) return rc;
     float* d_hidden = nullptr;
     if (hidden) d_hidden = reinterpret_cast<float*>(c->qkv);  // free after the forward; M*D*4 <= M*3*D*2
-    Outs o{c->d_logits, c->d_act, pooled ? c->d_pooled : nullptr, d_hidden};
+    const Outs o = staged_outs(c, (int)n, pooled ? c->d_pooled : nullptr, d_hidden);
     rc = launch_forward(c, b, o, c->stream);
     if (rc) return rc;
-    CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
-    if (G) CK(cudaMemcpyAsync(logits, c->d_logits, (size_t)G * 4, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaMemcpyAsync(act, c->d_act, (size_t)n * 8, cudaMemcpyDeviceToHost, c->stream));
     if (pooled) CK(cudaMemcpyAsync(pooled, c->d_pooled, (size_t)n * D * 4, cudaMemcpyDeviceToHost, c->stream));
     if (hidden) CK(cudaMemcpyAsync(hidden, d_hidden, (size_t)M * D * 4, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    rc = read_back(c, (int)n, G, logits, act);
+    if (rc) return rc;
     return read_err(c);
 }
 
@@ -782,7 +795,7 @@ int laya_gpu_forward_trace(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_
     Batch b;
     rc = stage_batch(c, &sq, 1, M, G, maxlen, &b);
     if (rc) return rc;
-    Outs o{c->d_logits, c->d_act, nullptr, nullptr};
+    const Outs o = staged_outs(c, 1, nullptr, nullptr);
     const size_t LD = (size_t)L * D;
     ActMaps am;
     rc = build_maps(c, M, &am);
@@ -790,10 +803,8 @@ int laya_gpu_forward_trace(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_
     TraceHook hook{c, trace, LD};
     cudaError_t e = run_forward(c, b, o, am, c->stream, hook);
     if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
-    CK(cudaMemcpyAsync(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
-    if (G) CK(cudaMemcpyAsync(logits, c->d_logits, (size_t)G * 4, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaMemcpyAsync(act, c->d_act, 8, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    rc = read_back(c, 1, G, logits, act);
+    if (rc) return rc;
     // The GPU fuses the final norm with the type embedding; the "final" tag
     // is recovered on the host as temb - type_emb[qtype].
     std::vector<float> te(3 * D);
@@ -817,7 +828,7 @@ int laya_gpu_forward_dump(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t
     Batch b;
     rc = stage_batch(c, &sq, 1, M, G, maxlen, &b);
     if (rc) return rc;
-    Outs o{c->d_logits, c->d_act, nullptr, nullptr};
+    const Outs o = staged_outs(c, 1, nullptr, nullptr);
     ActMaps am;
     rc = build_maps(c, M, &am);
     if (rc) return rc;

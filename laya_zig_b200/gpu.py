@@ -137,6 +137,28 @@ def option_probs(logits: np.ndarray, qtype: int, temperature: Sequence[float] = 
     return (p / p.sum()).astype(np.float32)
 
 
+class PreparedBatch:
+    """Decisions marshalled once into the C call's laya_seq array, with
+    output arrays, for callers that run the same host-buffer batch shape
+    again and again (LayaGPU.forward_prepared). The token ids stay in the
+    caller's host arrays: every call still copies them to the device and
+    the results back."""
+
+    def __init__(self, decisions):
+        self.n = len(decisions)
+        self.seqs = (_Seq * self.n)()
+        self._keep = []
+        G = 0
+        for i, d in enumerate(decisions):
+            ids, mk = _u32(d.ids), _u32(d.markers)
+            self._keep += [ids, mk]
+            self.seqs[i] = _Seq(ids.ctypes.data, len(ids), mk.ctypes.data if len(mk) else None, len(mk),
+                                int(d.qtype))
+            G += len(mk)
+        self.logits = np.zeros(max(G, 1), np.float32)
+        self.act = np.zeros((self.n, 2), np.float32)
+
+
 class LayaGPU:
     """One model replica on one GPU (one context per device)."""
 
@@ -215,6 +237,13 @@ class LayaGPU:
             g += K
             t += L
         return out
+
+    def forward_prepared(self, pb: PreparedBatch):
+        """laya_gpu_forward_batch on a PreparedBatch: returns (logits of all
+        markers in order, act[n][2]), the batch's own arrays, overwritten by
+        the next call."""
+        self._check(lib.laya_gpu_forward_batch(self._h, pb.seqs, pb.n, _p(pb.logits), _p(pb.act), None, None))
+        return pb.logits, pb.act
 
     def forward_trace(self, ids, qtype: int, markers):
         """(logits, act, trace[27][L][768]) -- the hidden state after every

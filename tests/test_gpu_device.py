@@ -51,3 +51,16 @@ def test_f16_precision_parity(weights, oracle_model):
         assert int(np.argmax(g.logits)) == int(np.argmax(r["logits"]))
     finally:
         m.close()
+
+
+def test_prepared_batch_equals_forward_batch(gpu_model):
+    """The prepared host-buffer call (used for the end-to-end timing) returns
+    what forward_batch returns, call after call."""
+    from laya_zig_b200 import gpu, synth
+    batch = synth.snake_batch(12, seed=9)
+    pb = gpu.PreparedBatch(batch)
+    ref = gpu_model.forward_batch(batch)
+    for _ in range(2):
+        logits, act = gpu_model.forward_prepared(pb)
+        np.testing.assert_array_equal(np.concatenate([h.logits for h in ref]), logits)
+        np.testing.assert_array_equal(np.stack([h.act for h in ref]), act)

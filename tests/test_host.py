@@ -112,3 +112,19 @@ def test_lpt_assignment_balances():
         flat = sorted(i for r in mine for b in r for i in b)
         assert flat == list(range(len(sw)))  # every decision exactly once
         assert max(loads) / (sum(loads) / world) < 1.15
+
+
+def test_prepared_batch_marshals_every_sequence():
+    """PreparedBatch points each laya_seq at the caller's arrays, in order."""
+    import ctypes
+    from laya_zig_b200 import gpu, synth
+    batch = synth.snake_batch(5, seed=3)
+    pb = gpu.PreparedBatch(batch)
+    assert pb.n == 5 and pb.act.shape == (5, 2)
+    assert len(pb.logits) == sum(len(d.markers) for d in batch)
+    for i, d in enumerate(batch):
+        sq = pb.seqs[i]
+        assert sq.len == len(d.ids) and sq.n_markers == len(d.markers) and sq.qtype == int(d.qtype)
+        ids = np.ctypeslib.as_array(ctypes.cast(sq.ids, ctypes.POINTER(ctypes.c_uint32)), shape=(sq.len,))
+        np.testing.assert_array_equal(ids, np.asarray(d.ids, np.uint32))
+
