@@ -299,7 +299,7 @@ def main():
         "config": config(world),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": tr,
-                     "kernel": "gemm_kernel (tcgen05 projection GEMMs, %d launches per step)" % gemm_launches,
+                     "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 projection GEMMs, %d launches per step)" % gemm_launches,
                      "peak_source": "%s bf16_tflops_sustained (%s)" % ("MEASURED_PEAKS.json" if src == "measured"
                                                                         else "fallback", src),
                      "algorithmic_flops_per_step": gemm_flops},
