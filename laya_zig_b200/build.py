@@ -2,8 +2,8 @@
 
     python -m laya_zig_b200.build [--verbose-ptxas] [--force]
 
-Each .cu under csrc/ compiles to an object in _build/ (in parallel, skipped
-when newer than its sources), then they link into laya_zig_b200/liblaya_gpu.so
+Each .cu (nvcc) and .cpp (g++, host-only) under csrc/ compiles to an
+object in _build/ (in parallel, skipped when newer than its sources), then they link into laya_zig_b200/liblaya_gpu.so
 with the CUDA runtime linked statically, so the library loads on a host
 without a GPU (the driver is resolved at first use).
 """
@@ -35,8 +35,11 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-pthread", "-Wall", "-I", os.path.join(ROOT, "include")]
+
+
 def _deps() -> list:
-    return glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(ROOT, "include", "laya_gpu.h")]
+    return glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
 
 
 def _compile(src: str, verbose_ptxas: bool, force: bool) -> str:
@@ -44,8 +47,11 @@ def _compile(src: str, verbose_ptxas: bool, force: bool) -> str:
     newest = max(os.path.getmtime(p) for p in [src] + _deps())
     if not force and os.path.exists(obj) and os.path.getmtime(obj) >= newest:
         return obj
-    cmd = [nvcc()] + ARCH + NVCC_FLAGS + ["-c", src, "-o", obj]
-    if verbose_ptxas:
+    if src.endswith(".cpp"):  # host-only C++ (the tokenizer)
+        cmd = ["g++"] + CXX_FLAGS + ["-c", src, "-o", obj]
+    else:
+        cmd = [nvcc()] + ARCH + NVCC_FLAGS + ["-c", src, "-o", obj]
+    if verbose_ptxas and not src.endswith(".cpp"):
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True, env={**os.environ, "CC": "gcc", "CXX": "g++"})
     if r.returncode != 0:
@@ -57,11 +63,11 @@ def _compile(src: str, verbose_ptxas: bool, force: bool) -> str:
 
 def build(verbose_ptxas: bool = False, force: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
-    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     with concurrent.futures.ThreadPoolExecutor(len(srcs)) as pool:
         objs = list(pool.map(lambda s: _compile(s, verbose_ptxas, force), srcs))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s%s" % (r.stdout, r.stderr))

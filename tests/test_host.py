@@ -10,15 +10,21 @@ from conftest import ROOT
 
 
 def _declared_symbols():
-    with open(os.path.join(ROOT, "include", "laya_gpu.h")) as f:
-        text = f.read()
-    return sorted(set(re.findall(r"LAYA_API\s+[\w\s\*]*?\b(laya_gpu_\w+)\s*\(", text)))
+    syms = set()
+    inc = os.path.join(ROOT, "include")
+    for name in sorted(os.listdir(inc)):
+        if name.endswith(".h"):
+            with open(os.path.join(inc, name)) as f:
+                syms |= set(re.findall(r"LAYA_(?:TOK_)?API\s+[\w\s\*]*?\b(laya_\w+)\s*\(", f.read()))
+    return sorted(syms)
 
 
 def test_library_loads_and_exports_every_declared_symbol():
+    """Every entry point of include/*.h (laya_gpu.h and laya_tok.h)."""
     from laya_zig_b200 import gpu
     syms = _declared_symbols()
-    assert len(syms) >= 12, syms
+    assert len(syms) >= 19, syms
+    assert any(s.startswith("laya_tok_") for s in syms)
     for s in syms:
         assert hasattr(gpu.lib, s), "liblaya_gpu.so does not export %s" % s
     assert gpu.lib.laya_gpu_version() == 1
