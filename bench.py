@@ -175,6 +175,100 @@ def run_reference(args, world):
     }), flush=True)
 
 
+def run_sweep(args, world: int):
+    """--workload sweep: the throughput sweep (65,536 decisions, lengths
+    uniform in [128, 512]) packed into length-sorted buckets of <= 32,768
+    tokens and spread over the ranks longest-processing-time first. Every
+    bucket of this rank is staged in HBM first; a step is one pass over all
+    of them, timed with CUDA events on the launching stream, max over ranks.
+    Total work is fixed, so the scaling is strong."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from laya_zig_b200 import gpu, shard, synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    weights = synth.make_weights(0)
+    model = gpu.LayaGPU.from_bf16(weights, device=local, precision=args.precision)
+    n = args.sweep_n
+    sw = synth.sweep_decisions(n, seed=4)
+    mine, _ = shard.shard(sw, world, rank)
+    staged, tokens, flops = [], 0, 0.0
+    for idx in mine:
+        dec = [sw[i] for i in idx]
+        p = gpu.pack(dec)
+        dev = {k: torch.from_numpy(v.view(np.int32)).cuda() for k, v in p.items() if k != "max_len"}
+        S, M, G = len(dec), len(p["ids"]), int(p["cu_markers"][-1])
+        db = gpu.DeviceBatch(dev["ids"].data_ptr(), dev["cu_seqlens"].data_ptr(), dev["markers"].data_ptr(),
+                             dev["cu_markers"].data_ptr(), dev["qtypes"].data_ptr(), S, M, G, p["max_len"])
+        staged.append((db, torch.zeros(max(G, 1), device="cuda"), torch.zeros((S, 2), device="cuda"), dev))
+        tokens += M
+        flops += shard.bucket_cost([len(d.ids) for d in dec])
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+    for _ in range(args.warmup):  # every bucket shape once: workspace growth, graphs for the small ones
+        for db, lg, ac, _ in staged:
+            model.forward_device(db, lg.data_ptr(), ac.data_ptr(), stream=sp)
+    model.sync()
+    barrier()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    clocks = Clocks([uuid] if uuid else [])
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        for db, lg, ac, _ in staged:
+            model.forward_device(db, lg.data_ptr(), ac.data_ptr(), stream=sp)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    model.sync()
+    for _, _, ac, _ in staged:
+        a = ac.cpu().numpy()
+        assert np.isfinite(a).all() and np.allclose(a.sum(1), 1, atol=1e-4), "bad act output"
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dist.destroy_process_group()
+    t_max = float(t.item())
+    model.close()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": "decisions/s (sweep: %d decisions, L 128-512)" % n, "value": n * args.steps / (t_max / 1e3),
+        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": args.precision, "data": "synthetic (seeded weights and token ids)",
+        "config": {"workload": "throughput sweep: %d decisions, lengths uniform in [128, 512], length-sorted "
+                               "buckets of <= 32,768 tokens, LPT over ranks" % n,
+                   "global_batch": n, "seq_len": "128-512", "parallelism": "replicas dp%d (no collective)" % world,
+                   "rank0_buckets": len(mine), "rank0_tokens": tokens,
+                   "l2": "every bucket's activations exceed L2"},
+        "rank0_tokens_per_s": tokens * args.steps / (t_max / 1e3),
+        "rank0_tflops": flops * args.steps / (t_max / 1e3) / 1e12,
+        "gpu_launches": len(mine) * 171 * args.steps,
+        "clocks": clk,
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -183,10 +277,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="snake", choices=["snake", "sweep"],
+                    help="snake: the 64 x 180 headline batch (default); sweep: the bucketed throughput sweep")
+    ap.add_argument("--sweep-n", type=int, default=65536)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference(args, world)
+        return
+    if args.workload == "sweep":
+        run_sweep(args, world)
         return
 
     import numpy as np

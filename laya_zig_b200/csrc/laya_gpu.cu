@@ -429,7 +429,22 @@ struct ProfileHook {
 
 // Run on stream s (any stream, the legacy default one included), capturing
 // a graph on the context's own stream on first use of this shape.
+// Batches above this many tokens run for milliseconds on the GPU, so
+// launching their 171 kernels directly costs under 1%; each distinct shape
+// would otherwise capture a graph that is rarely replayed (a length-bucketed
+// sweep has a new shape almost every bucket).
+constexpr int EAGER_TOKENS = 16384;
+
 int launch_forward(laya_ctx* c, const Batch& b, const Outs& o, cudaStream_t s) {
+    if (b.M > EAGER_TOKENS) {
+        ActMaps am;
+        int rc = build_maps(c, b.M, &am);
+        if (rc) return rc;
+        NoHook hook;
+        cudaError_t e = run_forward(c, b, o, am, s, hook);
+        if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward launch: %s", cudaGetErrorString(e));
+        return LAYA_OK;
+    }
     GraphKey k{b.M, b.S, b.G, b.maxlen, b.ids, b.cu, b.mk, b.cum, b.qt, o.logits, o.act, o.pooled, o.hidden};
     auto it = c->graphs.find(k);
     if (it == c->graphs.end()) {
