@@ -33,6 +33,7 @@ sys.path.insert(0, ROOT)
 METRIC = "decisions/s (180-tok, bs=64)"
 UNIT = "decisions/s"
 BATCH = 64
+D_MODEL = 768
 GEMM_PARAMS = 124_452_864          # projection weights per token (encoder 110,297,088 + head 14,155,776)
 FALLBACK = {"bf16_tflops_sustained": 1400.0, "bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 
@@ -381,7 +382,33 @@ def main():
     peak = float(pk.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"]))
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
     tr = traffic_per_launch()
-    flops_step = gemm_flops + sum(attn_flops(len(d.ids)) for d in batch)
+    attn_step = sum(attn_flops(len(d.ids)) for d in batch)
+    flops_step = gemm_flops + attn_step
+    # the other kernel families against their own bounds, same profiled pass
+    hbm = float(pk.get("hbm_gbs", FALLBACK["hbm_gbs"]))
+    hbm_src = "%s hbm_gbs (%s)" % ("MEASURED_PEAKS.json" if src == "measured" else "fallback", src)
+
+    def per_launch_ms(stage):
+        return stage_ms[stage] / 5 / max(1, launches[stage])
+
+    secondary = []
+    if launches.get("norm"):
+        ln_bytes = M * (D_MODEL * 4 + D_MODEL * 2)  # f32 row in, 16-bit row out
+        a = ln_bytes / (per_launch_ms("norm") / 1e3) / 1e9
+        secondary.append({"kernel": "ln_kernel (%d launches per step)" % launches["norm"], "bound": "hbm",
+                          "algorithmic_bytes_per_launch": ln_bytes, "achieved": a, "peak": hbm, "unit": "GB/s",
+                          "frac": a / hbm, "peak_source": hbm_src})
+    if launches.get("attention"):
+        a = attn_step / (stage_ms["attention"] / 5 / 1e3) / 1e12
+        secondary.append({"kernel": "attention_kernel (%d launches per step)" % launches["attention"],
+                          "bound": "tensor", "algorithmic_flops_per_step": attn_step, "achieved": a, "peak": peak,
+                          "unit": "TFLOP/s", "frac": a / peak})
+    for st, name, nbytes in (("embed", "embed_kernel", M * (D_MODEL * 2 + D_MODEL * 4 + D_MODEL * 2)),
+                             ("final", "final_kernel", M * (D_MODEL * 4 + D_MODEL * 4 + D_MODEL * 2))):
+        if launches.get(st):
+            a = nbytes / (per_launch_ms(st) / 1e3) / 1e9
+            secondary.append({"kernel": name, "bound": "hbm", "algorithmic_bytes_per_launch": nbytes, "achieved": a,
+                              "peak": hbm, "unit": "GB/s", "frac": a / hbm, "peak_source": hbm_src})
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -409,6 +436,7 @@ def main():
         "clocks": clk,
         "stage_ms_per_step": {k: v / 5 for k, v in stage_ms.items()},
         "whole_step_tflops": flops_step / (t_max / args.steps / 1e3) / 1e12,
+        "secondary_rooflines": secondary,
     }
     print(json.dumps(out), flush=True)
     model.close()
