@@ -297,7 +297,9 @@ class LayaGPU:
 
     def profile(self, batch: "DeviceBatch", logits_ptr: int, act_ptr: int, iters: int = 1, stream: int = 0):
         """--profile (src/main.zig:132-198): ({stage: summed kernel ms}, {stage: launches per forward})
-        over `iters` eager forwards timed with CUDA events around every kernel."""
+        over `iters` replays of a CUDA graph of one forward with an event pair
+        around every kernel (the events stop neighbouring kernels from
+        overlapping, so the times are upper bounds)."""
         ms = np.zeros(len(STAGES), np.float32)
         n = np.zeros(len(STAGES), np.int32)
         self._check(lib.laya_gpu_forward_profile(self._h, ctypes.byref(batch.c), logits_ptr or None, act_ptr or None,
