@@ -1,8 +1,9 @@
 // gemm.cu -- persistent tcgen05 GEMM for the projection layers.
 //
 // One CTA per SM, 320 threads, warp-specialised:
-//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per
-//               k-block into a STAGES-deep shared-memory ring (128B swizzle).
+//   warp 0      TMA producer: A tile [128 x 128] and B tile [BN x 128] per
+//               k-block, each as two 64-column boxes (128B swizzle), into a
+//               STAGES-deep shared-memory ring.
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
 //               K=16) into a double-buffered f32 accumulator in TMEM and
 //               commits to mbarriers (ring slot free / accumulator full).
@@ -29,16 +30,17 @@ namespace laya {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BK = 64;
+constexpr int BK = 128;    // K per pipeline stage
+constexpr int KSUB = 64;   // K per 128-byte-swizzled sub-tile (one TMA box wide)
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int STAGING_BYTES = 32 * 128;  // one 32-row x 128-byte output tile
-// Staging tiles per epilogue warp: two for the 16-bit epilogues, so one
-// drains to the TMA unit while the next fills; one for the f32 ones, whose
-// TMA reduce-adds are paced by L2 and gain more from a deeper operand ring.
+// Staging tiles per epilogue warp. One: with 64 KB operand stages (K = 128
+// per stage) a second tile per warp would leave room for only two stages,
+// and three stages with one tile measured faster (GLU 35.3 vs 37.2 us).
 template <int EPI>
 constexpr int staging_bufs() {
-    return (EPI == EPI_F32 || EPI == EPI_RESID) ? 1 : 2;
+    return 1;
 }
 constexpr int SMEM_LIMIT = 227 * 1024;
 
@@ -333,12 +335,18 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
                         // both CTAs' bytes complete on rank 0's barrier; only rank 0 arms it
                         const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
                         if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
-                        tma_load_2d_pair(sa, &a_map, bar, kb * BK, m0);
-                        tma_load_2d_pair(sa + C::A_BYTES, &b_map, bar, kb * BK, n0);
+                        for (int j = 0; j < BK / KSUB; j++) {
+                            tma_load_2d_pair(sa + j * BM * KSUB * 2, &a_map, bar, kb * BK + j * KSUB, m0);
+                            tma_load_2d_pair(sa + C::A_BYTES + j * C::B_ROWS * KSUB * 2, &b_map, bar,
+                                             kb * BK + j * KSUB, n0);
+                        }
                     } else {
                         mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-                        tma_load_2d(sa, &a_map, &full[stage], kb * BK, m0);
-                        tma_load_2d(sa + C::A_BYTES, &b_map, &full[stage], kb * BK, n0);
+                        for (int j = 0; j < BK / KSUB; j++) {
+                            tma_load_2d(sa + j * BM * KSUB * 2, &a_map, &full[stage], kb * BK + j * KSUB, m0);
+                            tma_load_2d(sa + C::A_BYTES + j * C::B_ROWS * KSUB * 2, &b_map, &full[stage],
+                                        kb * BK + j * KSUB, n0);
+                        }
                     }
                     issued_phase[stage] = (int)phase;
                     if (++stage == C::STAGES) {
@@ -383,11 +391,14 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
-                    const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + C::A_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; k++) {
-                        if constexpr (PAIR) tc_mma_f16_pair(d, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
-                        else tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, IDESC, (kb | k) != 0);
+                        // sub-tile k / 4 of the stage, 16-column step k % 4 inside it (32 B = 2 in the descriptor)
+                        const int j = k / (KSUB / 16), ks = k % (KSUB / 16);
+                        const uint64_t adesc = sw128_desc(sa + j * BM * KSUB * 2) + 2 * ks;
+                        const uint64_t bdesc = sw128_desc(sa + C::A_BYTES + j * C::B_ROWS * KSUB * 2) + 2 * ks;
+                        if constexpr (PAIR) tc_mma_f16_pair(d, adesc, bdesc, IDESC, (kb | k) != 0);
+                        else tc_mma_f16(d, adesc, bdesc, IDESC, (kb | k) != 0);
                     }
                     if constexpr (PAIR) tc_commit_pair(&empty[stage], 0x3);
                     else tc_commit(&empty[stage]);

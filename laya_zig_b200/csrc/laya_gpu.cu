@@ -901,7 +901,7 @@ int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, f
 int laya_gpu_linear(const void* x, const void* w, const float* bias, float* out, int M, int N, int K, int elem_dtype,
                     void* stream) {
     laya_ctx* c = nullptr;
-    if (!x || !w || !out || M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 64)
+    if (!x || !w || !out || M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128)
         return fail(c, LAYA_ERR_ARG, "linear: bad shape or NULL pointer (M=%d N=%d K=%d)", M, N, K);
     if (elem_dtype != LAYA_DT_BF16 && elem_dtype != LAYA_DT_F16)
         return fail(c, LAYA_ERR_DTYPE, "linear: elem_dtype %d", elem_dtype);
