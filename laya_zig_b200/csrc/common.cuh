@@ -290,6 +290,25 @@ inline bool pdl_enabled() {
     return on;
 }
 
+// An L2 access-policy window that every launch_k on this thread carries
+// while one is set (L2WindowScope): the forward marks the f32 residual
+// stream persisting, so it stays in L2 between the LayerNorms that read it
+// and the projections that add into it, while the other activations stream.
+struct L2Window {
+    void* base = nullptr;
+    size_t bytes = 0;
+    float hit_ratio = 0.f;
+};
+inline L2Window& l2_window() {
+    static thread_local L2Window w;
+    return w;
+}
+struct L2WindowScope {
+    L2Window saved;
+    explicit L2WindowScope(const L2Window& w) : saved(l2_window()) { l2_window() = w; }
+    ~L2WindowScope() { l2_window() = saved; }
+};
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                      Args&&... args) {
@@ -298,11 +317,25 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    if (pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        n++;
+    }
+    const L2Window& w = l2_window();
+    if (w.base && w.bytes) {
+        attr[n].id = cudaLaunchAttributeAccessPolicyWindow;
+        attr[n].val.accessPolicyWindow.base_ptr = w.base;
+        attr[n].val.accessPolicyWindow.num_bytes = w.bytes;
+        attr[n].val.accessPolicyWindow.hitRatio = w.hit_ratio;
+        attr[n].val.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+        attr[n].val.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+        n++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
