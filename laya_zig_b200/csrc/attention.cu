@@ -187,26 +187,48 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
         const int klo = kt * KB, khi = kt * KB + KB - 1;
         const bool need_mask = khi >= L || (window >= 0 && (q0 + QB - 1 - klo > window || khi - q0 > window));
         if (need_mask) {
+            // row qi sees keys [lo, hi]; element (j, e) of this thread holds
+            // key klo + 8j + 2(lane & 3) + e, so one unsigned compare of its
+            // offset from lo against hi - lo tests both ends
+            int lo0 = 0, hi0 = L - 1, lo1 = 0, hi1 = L - 1;
+            if (window >= 0) {
+                lo0 = max(0, qi0 - window);
+                hi0 = min(L - 1, qi0 + window);
+                lo1 = max(0, qi1 - window);
+                hi1 = min(L - 1, qi1 + window);
+            }
+            const int kb = klo + 2 * (lane & 3);
+            const int d0 = kb - lo0, d1 = kb - lo1;
+            // an empty range (a row past the sequence end, never stored) masks everything
+            const bool e0 = hi0 < lo0, e1 = hi1 < lo1;
+            const unsigned r0 = e0 ? 0u : (unsigned)(hi0 - lo0), r1 = e1 ? 0u : (unsigned)(hi1 - lo1);
 #pragma unroll
             for (int j = 0; j < 8; j++) {
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
-                    const int kj = klo + j * 8 + 2 * (lane & 3) + e;
-                    const bool ok0 = kj < L && (window < 0 || abs(qi0 - kj) <= window);
-                    const bool ok1 = kj < L && (window < 0 || abs(qi1 - kj) <= window);
-                    if (!ok0) s[j][e] = -INFINITY;
-                    if (!ok1) s[j][2 + e] = -INFINITY;
+                    if (e0 || (unsigned)(d0 + j * 8 + e) > r0) s[j][e] = -INFINITY;
+                    if (e1 || (unsigned)(d1 + j * 8 + e) > r1) s[j][2 + e] = -INFINITY;
                 }
             }
         }
         // online softmax over raw scores, two rows per thread (qi0, qi1);
         // p = 2^(s * log2(e)/8 - max * log2(e)/8)
-        float mx0 = -INFINITY, mx1 = -INFINITY;
+        // row maxima as balanced trees (depth 4, not a 16-long chain)
+        float ta[8], tb[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
-            mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+            ta[j] = fmaxf(s[j][0], s[j][1]);
+            tb[j] = fmaxf(s[j][2], s[j][3]);
         }
+#pragma unroll
+        for (int w = 4; w > 0; w >>= 1) {
+#pragma unroll
+            for (int j = 0; j < w; j++) {
+                ta[j] = fmaxf(ta[j], ta[j + w]);
+                tb[j] = fmaxf(tb[j], tb[j + w]);
+            }
+        }
+        float mx0 = ta[0], mx1 = tb[0];
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
