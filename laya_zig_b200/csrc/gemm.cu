@@ -86,11 +86,25 @@ __device__ __forceinline__ void load_cols(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void add_bias(float (&v)[32], const float* bias, int col) {
+// Two 16-column groups of this thread's row, one wait for both.
+__device__ __forceinline__ void load_cols16x2(uint32_t taddr0, uint32_t taddr1, float (&v0)[16], float (&v1)[16]) {
+    uint32_t r0[16], r1[16];
+    tmem_ld16(taddr0, r0);
+    tmem_ld16(taddr1, r1);
+    tc_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        v0[i] = __uint_as_float(r0[i]);
+        v1[i] = __uint_as_float(r1[i]);
+    }
+}
+
+template <int NV>
+__device__ __forceinline__ void add_bias(float (&v)[NV], const float* bias, int col) {
     if (bias) {
         const float4* b = reinterpret_cast<const float4*>(bias + col);
 #pragma unroll
-        for (int q = 0; q < 8; q++) {
+        for (int q = 0; q < NV / 4; q++) {
             const float4 t = __ldg(b + q);
             v[4 * q] += t.x;
             v[4 * q + 1] += t.y;
@@ -107,11 +121,11 @@ __device__ __forceinline__ uint4* stage_chunk(uint8_t* tile, int lane, int j) {
     return reinterpret_cast<uint4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4));
 }
 
-// 32 values -> 64 bytes of 16-bit elements at chunks [c0, c0 + 4).
-template <typename T>
-__device__ __forceinline__ void stage16(uint8_t* tile, int lane, int c0, const float (&v)[32]) {
+// NV values -> 2*NV bytes of 16-bit elements at chunks [c0, c0 + NV/8).
+template <typename T, int NV>
+__device__ __forceinline__ void stage16(uint8_t* tile, int lane, int c0, const float (&v)[NV]) {
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
+    for (int q = 0; q < NV / 8; q++) {
         uint4 u;
         u.x = Pack<T>::two(v[8 * q + 0], v[8 * q + 1]);
         u.y = Pack<T>::two(v[8 * q + 2], v[8 * q + 3]);
@@ -157,10 +171,23 @@ struct Staging {
     }
 };
 
+// EPI_QKV: (cos, sin) of row m0q + lane's position for the 32 frequencies,
+// from the frequency-major per-token rows: for each i the warp's 32
+// consecutive rows are 512 contiguous bytes. Rows past M are computed but
+// their stores are clipped; they read row 0.
+__device__ __forceinline__ void rope_load(const GemmArgs& a, int m0q, int lane, float4 (&cs)[16]) {
+    const int r = m0q + lane;
+    const float4* src = a.rope_tok + (r < a.M ? r : 0);
+#pragma unroll
+    for (int i = 0; i < 16; i++) cs[i] = __ldg(src + (size_t)i * a.rope_ld);
+}
+
+// cs: EPI_QKV's rope_load of this warp's rows (unused otherwise).
 template <int BN, int EPI, typename T>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* out_map,
                                               Staging<staging_bufs<EPI>()>& st,
-                                              uint32_t tacc, int half, int lane, int m0q, int n_blk) {
+                                              uint32_t tacc, int half, int lane, int m0q, int n_blk,
+                                              const float4 (&cs)[16]) {
     constexpr int HALF = BN / 2;  // accumulator columns this warp owns
     if constexpr (EPI == EPI_GLU) {
         // tile columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows;
@@ -182,37 +209,33 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
     } else if constexpr (EPI == EPI_QKV) {
         const int col0 = n_blk * BN + half * HALF;
         const bool rope = col0 < a.rope_cols;
-        float4 cs[16];  // (cos, sin) of this row's position for the 32 frequencies, loaded once per tile
-        if (rope) {
-            const int r = m0q + lane;
-            const int p = r < a.M ? a.pos[r] : 0;  // rows past M are computed but their stores are clipped
-            const float4* src = reinterpret_cast<const float4*>(a.rope + (size_t)p * 32);
-#pragma unroll
-            for (int i = 0; i < 16; i++) cs[i] = __ldg(src + i);
-        }
 #pragma unroll 1
         for (int c = 0; c < HALF; c += 64) {
-            float x0[32], x1[32];
-            load_cols(tacc + half * HALF + c, x0);
-            load_cols(tacc + half * HALF + c + 32, x1);
+            // one head (64 columns): rotate_half pairs column d with d + 32
+            // (src/main.zig:2512-2519); done in two passes of 16 frequencies
+            // so that only 32 accumulator values are live beside the pairs
             const int col = col0 + c;
-            add_bias(x0, a.bias, col);
-            add_bias(x1, a.bias, col + 32);
-            if (rope) {
-                // rotate_half pairing (d, d+32) within the head, src/main.zig:2512-2519
-#pragma unroll
-                for (int d = 0; d < 32; d += 2) {
-                    const float4 t = cs[d / 2];  // (cos d, sin d, cos d+1, sin d+1)
-                    const float a0 = x0[d], b0 = x1[d], a1 = x0[d + 1], b1 = x1[d + 1];
-                    x0[d] = a0 * t.x - b0 * t.y;
-                    x1[d] = b0 * t.x + a0 * t.y;
-                    x0[d + 1] = a1 * t.z - b1 * t.w;
-                    x1[d + 1] = b1 * t.z + a1 * t.w;
-                }
-            }
             uint8_t* tile = st.next(lane);
-            stage16<T>(tile, lane, 0, x0);
-            stage16<T>(tile, lane, 4, x1);
+#pragma unroll
+            for (int hq = 0; hq < 2; hq++) {
+                float x0[16], x1[16];
+                load_cols16x2(tacc + half * HALF + c + 16 * hq, tacc + half * HALF + c + 32 + 16 * hq, x0, x1);
+                add_bias(x0, a.bias, col + 16 * hq);
+                add_bias(x1, a.bias, col + 32 + 16 * hq);
+                if (rope) {
+#pragma unroll
+                    for (int d = 0; d < 16; d += 2) {
+                        const float4 t = cs[8 * hq + d / 2];  // (cos, sin) of frequencies 16hq+d, 16hq+d+1
+                        const float a0 = x0[d], b0 = x1[d], a1 = x0[d + 1], b1 = x1[d + 1];
+                        x0[d] = a0 * t.x - b0 * t.y;
+                        x1[d] = b0 * t.x + a0 * t.y;
+                        x0[d + 1] = a1 * t.z - b1 * t.w;
+                        x1[d + 1] = b1 * t.z + a1 * t.w;
+                    }
+                }
+                stage16<T>(tile, lane, 2 * hq, x0);
+                stage16<T>(tile, lane, 4 + 2 * hq, x1);
+            }
             flush_stage<false>(out_map, tile, lane, col, m0q);
         }
     } else if constexpr (EPI == EPI_F32 || EPI == EPI_RESID) {
@@ -433,14 +456,20 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
         for (int t = unit; t < total; t += units, it++) {
             const int buf = it & 1;
             const uint32_t tph = (it >> 1) & 1;
+            const int m0q = (t / tiles_n) * TILE_M + (int)rank * BM + q * 32;
+            // the RoPE pairs are requested before the accumulator wait, so
+            // their latency overlaps the tile's MMAs
+            float4 cs[16];
+            if constexpr (EPI == EPI_QKV) {
+                if ((t % tiles_n) * BN + half * (BN / 2) < args.rope_cols) rope_load(args, m0q, lane, cs);
+            }
             int ok = 1;
             if (lane == 0) ok = mbar_wait(&tfull[buf], tph, args.err, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const int m0q = (t / tiles_n) * TILE_M + (int)rank * BM + q * 32;
             const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-            epilogue_tile<BN, EPI, T>(args, &out_map, st, tacc, half, lane, m0q, t % tiles_n);
+            epilogue_tile<BN, EPI, T>(args, &out_map, st, tacc, half, lane, m0q, t % tiles_n, cs);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {

@@ -21,8 +21,8 @@ enum Epilogue : int {
 struct GemmArgs {
     int M, N, K;
     const float* bias;      // [N] or null
-    const int* pos;         // EPI_QKV: RoPE position of each row
-    const float2* rope;     // EPI_QKV: [MAX_POS][32] (cos, sin)
+    const float4* rope_tok; // EPI_QKV: [16][rope_ld], (cos, sin) of frequencies 2i, 2i+1 for row r at [i][r]
+    int rope_ld;
     int rope_cols;          // EPI_QKV: RoPE applies to columns [0, rope_cols)
     int* err;               // device error word
 };

@@ -5,8 +5,11 @@
 namespace laya {
 
 // norm.cu ------------------------------------------------------------------
+// rope: the [MAX_POS][32] (cos, sin) table; rope_tok: [16][rope_ld] float4,
+// row i of token t = (cos, sin) of frequencies 2i and 2i+1 at t's position.
 cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_seqs, int M, const void* emb,
-                         const float* w, float* x, void* xn, int* pos, int* seq_of, int* err, cudaStream_t s);
+                         const float* w, float* x, void* xn, const float2* rope, float4* rope_tok, int rope_ld,
+                         int* seq_of, int* err, cudaStream_t s);
 cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, int num_sms,
                       cudaStream_t s);
 cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const float* type_emb,

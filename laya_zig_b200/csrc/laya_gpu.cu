@@ -85,7 +85,8 @@ struct laya_ctx {
     std::vector<void*> ws;
     float* x = nullptr;
     void *xn = nullptr, *qkv = nullptr, *ctxb = nullptr, *mlp = nullptr, *ff = nullptr;
-    int *pos = nullptr, *seq_of = nullptr;
+    float4* rope_tok = nullptr;  // [16][capM]: per-token RoPE pairs, frequency-major
+    int* seq_of = nullptr;
     float *mv = nullptr, *partial = nullptr;
     // Staged batch inputs / outputs of the host-buffer entry points. d_in
     // holds ids | cu_seqlens | qtypes | markers | cu_markers packed for the
@@ -205,7 +206,7 @@ int ensure_workspace(laya_ctx* c, int M, int S, int G) {
     A(&c->ctxb, (size_t)nM * D * e16);
     A(&c->mlp, (size_t)nM * INTER * e16);
     A(&c->ff, (size_t)nM * HEAD_FF * e16);
-    A((void**)&c->pos, (size_t)nM * 4);
+    A((void**)&c->rope_tok, (size_t)nM * 16 * sizeof(float4));
     A((void**)&c->seq_of, (size_t)nM * 4);
     A((void**)&c->mv, (size_t)nG * D * 4);
     A((void**)&c->partial, (size_t)nG * SCORER_GROUPS * 4);
@@ -269,8 +270,8 @@ cudaError_t gemm(laya_ctx* c, int epi, const CUtensorMap& a, const CUtensorMap& 
     g.N = N;
     g.K = K;
     g.bias = bias;
-    g.pos = c->pos;
-    g.rope = c->rope;
+    g.rope_tok = c->rope_tok;
+    g.rope_ld = c->capM;
     g.rope_cols = rope_cols;
     g.err = c->d_err;
     return launch_gemm(epi, 256, c->bf16, a, b, out, g, c->num_sms, s);
@@ -297,7 +298,8 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
     }
     L2WindowScope l2scope(l2w);
     RUN(LAYA_STAGE_EMBED,
-        launch_embed(c->bf16, b.ids, b.cu, b.S, M, c->emb, c->emb_norm, c->x, c->xn, c->pos, c->seq_of, c->d_err, s));
+        launch_embed(c->bf16, b.ids, b.cu, b.S, M, c->emb, c->emb_norm, c->x, c->xn, c->rope, c->rope_tok, c->capM,
+                     c->seq_of, c->d_err, s));
     hook.tap(0);
     for (int l = 0; l < NL; l++) {
         const EncW& w = c->enc[l];

@@ -120,12 +120,16 @@ __device__ __forceinline__ int find_seq(const int* cu, int n, int t) {
 }
 
 // embedJob + normJob (src/main.zig:2543-2555): x = LN(E[id]); also writes the
-// 16-bit copy layer 0 multiplies (its attn_norm is the identity) and, per
-// token, its position in its sequence and the sequence index.
+// 16-bit copy layer 0 multiplies (its attn_norm is the identity), the
+// sequence index of each token, and the RoPE (cos, sin) pairs of the token's
+// position (src/main.zig:2503-2506) transposed to frequency-major rows
+// rope_tok[i][t], so the QKV projection's epilogue, where lane l holds
+// token m0 + l, reads them with coalesced loads and no position lookup.
 template <typename T>
 __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ cu, int n_seqs, int M,
                              const T* __restrict__ emb, const float* __restrict__ w, float* __restrict__ x,
-                             T* __restrict__ xn, int* __restrict__ pos, int* __restrict__ seq_of, int* err) {
+                             T* __restrict__ xn, const float2* __restrict__ rope, float4* __restrict__ rope_tok,
+                             int rope_ld, int* __restrict__ seq_of, int* err) {
     griddep_wait();
     griddep_launch();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -136,11 +140,19 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* __rest
         if (lane == 0) atomicOr(err, ERR_BAD_INDEX);
         id = 0;
     }
+    int p = 0;
     if (lane == 0) {
         const int s = find_seq(cu, n_seqs, t);
         seq_of[t] = s;
-        pos[t] = t - cu[s];
+        p = t - cu[s];
+        if (p >= MAX_POS) {  // sequence lengths are checked on the host; never read past the table
+            atomicOr(err, ERR_BAD_INDEX);
+            p = 0;
+        }
     }
+    p = __shfl_sync(0xffffffffu, p, 0);
+    if (lane < 16)
+        rope_tok[(size_t)lane * rope_ld + t] = reinterpret_cast<const float4*>(rope + (size_t)p * 32)[lane];
     Row r;
     load16_row<T>(r, emb + (size_t)id * D, lane);
     layer_norm(r, w, nullptr, lane);
@@ -217,16 +229,18 @@ constexpr int ROWS_PER_BLOCK = 8;  // 256 threads
 }  // namespace
 
 cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_seqs, int M, const void* emb,
-                         const float* w, float* x, void* xn, int* pos, int* seq_of, int* err, cudaStream_t s) {
+                         const float* w, float* x, void* xn, const float2* rope, float4* rope_tok, int rope_ld,
+                         int* seq_of, int* err, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
     const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
     if (bf16)
         return launch_k(embed_kernel<__nv_bfloat16>, grid, 32 * ROWS_PER_BLOCK, 0, s, ids, cu, n_seqs, M,
-                        static_cast<const __nv_bfloat16*>(emb), w, x, static_cast<__nv_bfloat16*>(xn), pos, seq_of,
-                        err);
+                        static_cast<const __nv_bfloat16*>(emb), w, x, static_cast<__nv_bfloat16*>(xn), rope, rope_tok,
+                        rope_ld, seq_of, err);
     else
         return launch_k(embed_kernel<__half>, grid, 32 * ROWS_PER_BLOCK, 0, s, ids, cu, n_seqs, M,
-                        static_cast<const __half*>(emb), w, x, static_cast<__half*>(xn), pos, seq_of, err);
+                        static_cast<const __half*>(emb), w, x, static_cast<__half*>(xn), rope, rope_tok, rope_ld, seq_of,
+                        err);
     return cudaGetLastError();
 }
 
