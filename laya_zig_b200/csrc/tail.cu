@@ -4,7 +4,8 @@
 //   marker_ln   x[marker token] -> LayerNorm(scorer.0 w, b)        (2761-2763)
 //   scorer      h = gelu(scorer.1 . v + b); partial dot with scorer.3 over
 //               each group of 64 outputs, summed later in a fixed order
-//               (2764-2767), so the result does not depend on scheduling
+//               (2764-2767), so the result does not depend on scheduling;
+//               K split over a cluster of 4 CTAs, reduced in rank order
 //   act         per sequence: logits, pooled = x[CLS], untempered softmax,
 //               [top1, top1-top2, entropy/ln(max(K,2)), max(K,2)/255],
 //               [pooled | features] -> 256 -> gelu -> 2 -> softmax (2787-2814)
@@ -69,37 +70,55 @@ __global__ void marker_ln_kernel(const float* __restrict__ x, const int* __restr
     }
 }
 
-// scorer.1 + gelu + dot with scorer.3, as an f32 tile GEMM: a CTA takes 32
-// markers x 64 scorer outputs, each of its 256 threads 2 markers x 4 outputs;
-// k-chunks of 32 are staged in shared memory and the next chunk's loads are
-// issued before the current chunk's FMAs. The CTA's 64 outputs of a marker
-// are summed (after gelu and the scorer.3 weights) into one partial sum.
-constexpr int SC_M = 32, SC_N = 64, SC_K = 32;
-__global__ void __launch_bounds__(256) scorer_kernel(const float* __restrict__ mv, int G, const float* __restrict__ w1,
-                                                     const float* __restrict__ b1, const float* __restrict__ w3,
-                                                     float* __restrict__ partial) {
+// scorer.1 + gelu + dot with scorer.3, as an f32 tile GEMM: a cluster of
+// SC_SPLIT CTAs takes 32 markers x 64 scorer outputs, CTA z of the cluster
+// the K range [z*192, z*192 + 192), each of its 256 threads 2 markers x 4
+// outputs; k-chunks of 32 are staged in shared memory and the next chunk's
+// loads are issued before the current chunk's FMAs. The partial tiles meet
+// in rank 0 through distributed shared memory, summed in rank order (a fixed
+// order, so results do not depend on scheduling), and rank 0 sums the
+// tile's 64 outputs of a marker (after gelu and the scorer.3 weights) into
+// one partial sum. Splitting K gives SC_SPLIT times the CTAs of a 32 x 64
+// tiling (768 for 512 markers), enough warps per SM to hide the shared
+// memory and FMA latencies.
+constexpr int SC_M = 32, SC_N = 64, SC_K = 32, SC_SPLIT = 4, SC_KR = D / SC_SPLIT;
+static_assert(SC_KR % SC_K == 0, "scorer K split");
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+__global__ void __cluster_dims__(1, 1, SC_SPLIT) __launch_bounds__(256)
+    scorer_kernel(const float* __restrict__ mv, int G, const float* __restrict__ w1, const float* __restrict__ b1,
+                  const float* __restrict__ w3, float* __restrict__ partial) {
     __shared__ float As[SC_K][SC_M + 4];  // [k][marker]
     __shared__ float Bs[SC_K][SC_N + 4];  // [k][output]
-    const int g0 = blockIdx.x * SC_M, j0 = blockIdx.y * SC_N;
+    __shared__ float4 red[2][256];        // this CTA's partial tile, by thread
+    const int g0 = blockIdx.x * SC_M, j0 = blockIdx.y * SC_N, kbeg = blockIdx.z * SC_KR;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;  // outputs tx*4.., markers ty*2..
     // loads: A 32x32 -> 4 floats per thread, B 64x32 -> 8 floats per thread
     const int ar = tid >> 3, ac = (tid & 7) * 4;        // A row (marker) 0..31, k offset
     const int br = tid >> 2, bc = (tid & 3) * 8;        // B row (output) 0..63, k offset
     const bool a_ok = g0 + ar < G;
-    const float* ap = mv + (size_t)(a_ok ? g0 + ar : 0) * D + ac;
-    const float* bp = w1 + (size_t)(j0 + br) * D + bc;
+    const float* ap = mv + (size_t)(a_ok ? g0 + ar : 0) * D + kbeg + ac;
+    const float* bp = w1 + (size_t)(j0 + br) * D + kbeg + bc;
     griddep_launch();
     float4 rb0 = *reinterpret_cast<const float4*>(bp), rb1 = *reinterpret_cast<const float4*>(bp + 4);  // weights
     griddep_wait();  // mv comes from the marker LayerNorm
     float4 ra = a_ok ? *reinterpret_cast<const float4*>(ap) : make_float4(0.f, 0.f, 0.f, 0.f);
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    for (int k0 = 0; k0 < D; k0 += SC_K) {
+    for (int k0 = 0; k0 < SC_KR; k0 += SC_K) {
         __syncthreads();
         As[ac + 0][ar] = ra.x; As[ac + 1][ar] = ra.y; As[ac + 2][ar] = ra.z; As[ac + 3][ar] = ra.w;
         Bs[bc + 0][br] = rb0.x; Bs[bc + 1][br] = rb0.y; Bs[bc + 2][br] = rb0.z; Bs[bc + 3][br] = rb0.w;
         Bs[bc + 4][br] = rb1.x; Bs[bc + 5][br] = rb1.y; Bs[bc + 6][br] = rb1.z; Bs[bc + 7][br] = rb1.w;
         __syncthreads();
-        if (k0 + SC_K < D) {  // next chunk in flight while this one is consumed
+        if (k0 + SC_K < SC_KR) {  // next chunk in flight while this one is consumed
             ra = a_ok ? *reinterpret_cast<const float4*>(ap + k0 + SC_K) : make_float4(0.f, 0.f, 0.f, 0.f);
             rb0 = *reinterpret_cast<const float4*>(bp + k0 + SC_K);
             rb1 = *reinterpret_cast<const float4*>(bp + k0 + SC_K + 4);
@@ -114,20 +133,37 @@ __global__ void __launch_bounds__(256) scorer_kernel(const float* __restrict__ m
             acc[1][2] = fmaf(av.y, bv.z, acc[1][2]); acc[1][3] = fmaf(av.y, bv.w, acc[1][3]);
         }
     }
+    red[0][tid] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+    red[1][tid] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+    cluster_sync();
+    if (cluster_rank() == 0) {
 #pragma unroll
-    for (int i = 0; i < 2; i++) {
-        float p = 0.f;
+        for (int r = 1; r < SC_SPLIT; r++) {
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int j = j0 + tx * 4 + c;
-            p += gelu_scalar(acc[i][c] + b1[j]) * w3[j];
+            for (int i = 0; i < 2; i++) {
+                const float4 v = ld_cluster_f4(mapa_shared(smem_u32(&red[i][tid]), r));
+                acc[i][0] += v.x;
+                acc[i][1] += v.y;
+                acc[i][2] += v.z;
+                acc[i][3] += v.w;
+            }
         }
-        // the 16 threads sharing a marker are 16 consecutive lanes
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-        const int g = g0 + ty * 2 + i;
-        if (tx == 0 && g < G) partial[(size_t)g * SCORER_GROUPS + blockIdx.y] = p;
+        for (int i = 0; i < 2; i++) {
+            float p = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int j = j0 + tx * 4 + c;
+                p += gelu_scalar(acc[i][c] + b1[j]) * w3[j];
+            }
+            // the 16 threads sharing a marker are 16 consecutive lanes
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+            const int g = g0 + ty * 2 + i;
+            if (tx == 0 && g < G) partial[(size_t)g * SCORER_GROUPS + blockIdx.y] = p;
+        }
     }
+    cluster_sync();  // the other ranks keep their shared memory until rank 0 has read it
 }
 
 // One CTA (1024 threads) per sequence: logits from the partial sums, pooled
@@ -242,8 +278,8 @@ cudaError_t launch_tail(const float* x, const int* cu_seqlens, const uint32_t* m
         cudaError_t e = launch_k(marker_ln_kernel, (G + 7) / 8, 256, 0, s, x, cu_seqlens, markers, cu_markers, n_seqs,
                                  G, w.s0w, w.s0b, mv, err);
         if (e != cudaSuccess) return e;
-        e = launch_k(scorer_kernel, dim3((G + SC_M - 1) / SC_M, D / SC_N), 256, 0, s, mv, G, w.s1w, w.s1b, w.s3w,
-                     partial);
+        e = launch_k(scorer_kernel, dim3((G + SC_M - 1) / SC_M, D / SC_N, SC_SPLIT), 256, 0, s, mv, G, w.s1w, w.s1b,
+                     w.s3w, partial);
         if (e != cudaSuccess) return e;
     }
     return launch_k(act_kernel, n_seqs, ACT_THREADS, 0, s, x, cu_seqlens, cu_markers, partial, w, logits, act,
