@@ -38,11 +38,25 @@ GEMM_PARAMS = 124_452_864          # projection weights per token (encoder 110,2
 FALLBACK = {"bf16_tflops_sustained": 1400.0, "bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 
 
+def l2_bytes() -> int:
+    """The current device's L2 size (126 MB on a B200; 0 without a GPU)."""
+    import torch
+    if not torch.cuda.is_available():
+        return 0
+    return int(torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size)
+
+
+def flush_bytes() -> int:
+    """Bytes written between timed steps to flush L2: 1.25x its size, in MiB."""
+    return ((l2_bytes() * 5 // 4) + (1 << 20) - 1) >> 20 << 20
+
+
 def config(world: int):
     return {"workload": "batched Snake-style decisions: 64 seqs x 175-180 tokens (uniform), 8 option markers, "
                         "act head on [CLS]; mmBERT-base 22 layers + 2 head layers",
             "global_batch": BATCH * world, "seq_len": 180, "parallelism": "replicas dp%d (no collective)" % world,
-            "l2": "flushed between timed steps (256 MB write)"}
+            "l2": "flushed between timed steps (%d MB write, 1.25x the %d MB L2)" % (flush_bytes() // 10**6,
+                                                                                l2_bytes() // 10**6)}
 
 
 def attn_flops(L: int) -> float:
@@ -316,7 +330,7 @@ def main():
                          dev["cu_markers"].data_ptr(), dev["qtypes"].data_ptr(), S, M, G, p["max_len"])
     logits = torch.zeros(G, dtype=torch.float32, device="cuda")
     act = torch.zeros((S, 2), dtype=torch.float32, device="cuda")
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = torch.empty(flush_bytes(), dtype=torch.uint8, device="cuda")
     torch.cuda.synchronize()
     stream = torch.cuda.Stream()          # every launch, flush and event of the timed loop goes here
     torch.cuda.set_stream(stream)
