@@ -337,6 +337,18 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // The weights (B) do not depend on the previous kernel. When every CTA
+    // (pair) has at most one tile (small M: a few SMs stream each
+    // projection's weights), the producer asks for its tile's B boxes in L2
+    // now, so their HBM latency overlaps the previous kernel's tail
+    // (single decisions 2.6-3% faster). With more tiles than CTAs the
+    // prefetched boxes only displace live activations from L2 (0.8% slower
+    // on a 64 x 180 batch), so there is none.
+    if (warp == 0 && lane == 0 && unit < total && total <= units) {
+        const int n0 = (unit % tiles_n) * BN + (int)rank * C::B_ROWS;
+        for (int kb = 0; kb < nk; kb++)
+            for (int j = 0; j < BK / KSUB; j++) tma_prefetch_l2_2d(&b_map, kb * BK + j * KSUB, n0);
+    }
     // Set-up above overlaps the previous kernel's tail; operands and outputs
     // are touched only after it has completed.
     griddep_launch();

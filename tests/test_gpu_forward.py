@@ -118,6 +118,34 @@ def test_batch_equals_single(gpu_model):
         np.testing.assert_array_equal(s.pooled, b.pooled)
 
 
+def test_batch_without_markers(gpu_model, oracle_model):
+    """A batch in which no sequence has an option marker: the scorer kernels
+    are not launched and the act head sees K = 0 (features of an empty
+    softmax, max(K, 2) = 2)."""
+    from laya_zig_b200 import synth
+    rng = np.random.Generator(np.random.PCG64(31))
+    cases = [synth._decision(rng, L, [], qt) for L, qt in [(1, 0), (40, 1), (181, 2)]]
+    outs = gpu_model.forward_batch(cases, want_pooled=True, want_hidden=True)
+    for d, g in zip(cases, outs):
+        assert len(g.logits) == 0
+        r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+        _compare(g, r, "L=%d K=0" % len(d.ids))
+
+
+def test_repeated_forward_bit_identical(gpu_model):
+    """Every reduction on the path runs in a fixed order (split-K scorer
+    partials in cluster-rank order, column-group partials, warp trees), so
+    the same batch gives the same bits every time."""
+    from laya_zig_b200 import synth
+    batch = synth.snake_batch(16, seed=13)
+    a = gpu_model.forward_batch(batch, want_pooled=True)
+    b = gpu_model.forward_batch(batch, want_pooled=True)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x.logits, y.logits)
+        np.testing.assert_array_equal(x.act, y.act)
+        np.testing.assert_array_equal(x.pooled, y.pooled)
+
+
 def test_ragged_and_edge_sequences(gpu_model, oracle_model):
     """Lengths around the tile and window edges, one token, no markers, every qtype."""
     from laya_zig_b200 import synth
