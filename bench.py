@@ -416,7 +416,9 @@ def main():
         a = attn_step / (stage_ms["attention"] / 5 / 1e3) / 1e12
         secondary.append({"kernel": "attention_kernel (%d launches per step)" % launches["attention"],
                           "bound": "tensor", "algorithmic_flops_per_step": attn_step, "achieved": a, "peak": peak,
-                          "unit": "TFLOP/s", "frac": a / peak})
+                          "unit": "TFLOP/s", "frac": a / peak,
+                          "peak_source": "%s bf16_tflops_sustained (%s)" % (
+                              "MEASURED_PEAKS.json" if src == "measured" else "fallback", src)})
     for st, name, nbytes in (("embed", "embed_kernel", M * (D_MODEL * 2 + D_MODEL * 4 + D_MODEL * 2)),
                              ("final", "final_kernel", M * (D_MODEL * 4 + D_MODEL * 4 + D_MODEL * 2))):
         if launches.get(st):
