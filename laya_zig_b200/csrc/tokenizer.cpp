@@ -27,6 +27,7 @@
 #include <cstring>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <vector>
 
 #include "laya_tok.h"
@@ -282,6 +283,7 @@ inline bool sep_at(const std::string& t, size_t i) {
 
 struct laya_tok {
     StrMap vocab, merges, added;
+    uint64_t serial = 0;  // unique per loaded tokenizer: keys the per-thread piece cache
     std::vector<size_t> added_lens;  // distinct, longest first
     bool start_byte[256] = {};
     uint32_t byte_ids[256] = {};
@@ -449,8 +451,46 @@ void laya_tok::finish() {  // finishTokenizer (main.zig:2000-2043)
     }
 }
 
+namespace {
+
+// Per-thread cache of BPE results, piece bytes -> ids. bpePiece is a pure
+// function of the tokenizer's tables and the piece, and text repeats its
+// words (a Snake board most of all), so a hit skips the merge loop; the ids
+// are the same either way. Entries belong to one tokenizer (its serial, not
+// its address, which a later tokenizer may reuse); pieces longer than
+// PIECE_CACHE_BYTES are not cached, and the cache is emptied when it holds
+// PIECE_CACHE_ENTRIES. Thread-local, so the threads of laya_tok_build_batch
+// need no lock.
+constexpr size_t PIECE_CACHE_BYTES = 64;
+constexpr size_t PIECE_CACHE_ENTRIES = 1 << 16;
+std::atomic<uint64_t> g_tok_serial{1};
+
+struct PieceCache {
+    uint64_t owner = 0;
+    std::unordered_map<std::string, std::vector<uint32_t>> map;
+};
+thread_local PieceCache t_piece_cache;
+
+}  // namespace
+
 void laya_tok::bpe_piece(const char* p, size_t n, std::vector<uint32_t>& out) const {  // main.zig:2111-2156
     if (n == 0) return;
+    PieceCache* pc = nullptr;
+    std::string ckey;
+    if (n <= PIECE_CACHE_BYTES) {
+        pc = &t_piece_cache;
+        if (pc->owner != serial) {
+            pc->map.clear();
+            pc->owner = serial;
+        }
+        ckey.assign(p, n);
+        const auto it = pc->map.find(ckey);
+        if (it != pc->map.end()) {
+            out.insert(out.end(), it->second.begin(), it->second.end());
+            return;
+        }
+    }
+    const size_t first_out = out.size();
     struct Sym {
         uint32_t a, b;  // [a, b) within the piece
     };
@@ -490,6 +530,10 @@ void laya_tok::bpe_piece(const char* p, size_t n, std::vector<uint32_t>& out) co
         } else {
             for (uint32_t i = s.a; i < s.b; i++) out.push_back(byte_ids[(uint8_t)p[i]]);
         }
+    }
+    if (pc) {
+        if (pc->map.size() >= PIECE_CACHE_ENTRIES) pc->map.clear();
+        pc->map.emplace(std::move(ckey), std::vector<uint32_t>(out.begin() + (long)first_out, out.end()));
     }
 }
 
@@ -680,6 +724,7 @@ LAYA_TOK_API int laya_tok_load(const char* path, laya_tok** out) {
         return fail(LAYA_TOK_ERR_IO, "out of host memory reading %s", path);
     }
     t->finish();
+    t->serial = g_tok_serial.fetch_add(1);
     *out = t;
     return LAYA_TOK_OK;
 }

@@ -231,3 +231,36 @@ def test_synthetic_vocabulary(synth_paths):
     for s in texts:
         assert t.encode(s) == o.encode(s), repr(s)
     t.close()
+
+
+def test_piece_cache_is_per_tokenizer(tmp_path):
+    """The library caches BPE results per host thread; the entries belong to
+    one loaded tokenizer. Two vocabularies that give the same pieces
+    different ids, used in turn on the same thread, and a tokenizer loaded
+    after another was destroyed (possibly at the same address), each give
+    their own ids."""
+    from laya_zig_b200 import tok as T
+    from oracle.tokenizer import Tokenizer
+    other = SYNTH.replace('"▁ab": 15', '"▁ab": 115').replace('"abc": 21', '"abc": 121').replace('"▁a": 14', '"▁a": 114')
+    assert other != SYNTH
+    pa, pb = tmp_path / "a.json", tmp_path / "b.json"
+    pa.write_text(SYNTH)
+    pb.write_text(other)
+    texts = ["ab", "abc abc ab", "a b c", "ab<mask>ab", "éé ab"]
+    oa, ob = Tokenizer(str(pa)), Tokenizer(str(pb))
+    ta, tb = T.Tokenizer(str(pa)), T.Tokenizer(str(pb))
+    for _ in range(3):
+        for s in texts:
+            assert ta.encode(s) == oa.encode(s), s
+            assert tb.encode(s) == ob.encode(s), s
+    assert ta.encode("ab") != tb.encode("ab")
+    ta.close()
+    tc = T.Tokenizer(str(pb))
+    for s in texts:
+        assert tc.encode(s) == ob.encode(s), s
+    tb.close()
+    ta2 = T.Tokenizer(str(pa))
+    for s in texts:
+        assert ta2.encode(s) == oa.encode(s), s
+    tc.close()
+    ta2.close()
