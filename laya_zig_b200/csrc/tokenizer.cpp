@@ -26,8 +26,8 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <cstdlib>
 #include <thread>
-#include <unordered_map>
 #include <vector>
 
 #include "laya_tok.h"
@@ -456,18 +456,35 @@ namespace {
 // Per-thread cache of BPE results, piece bytes -> ids. bpePiece is a pure
 // function of the tokenizer's tables and the piece, and text repeats its
 // words (a Snake board most of all), so a hit skips the merge loop; the ids
-// are the same either way. Entries belong to one tokenizer (its serial, not
-// its address, which a later tokenizer may reuse); pieces longer than
-// PIECE_CACHE_BYTES are not cached, and the cache is emptied when it holds
-// PIECE_CACHE_ENTRIES. Thread-local, so the threads of laya_tok_build_batch
+// are the same either way. Direct-mapped and allocation-free: PIECE_SLOTS
+// slots (~0.9 MB per thread, allocated on the thread's first piece), each
+// holding one piece of up to PIECE_BYTES bytes with its ids (at most
+// PIECE_IDS), tagged with the serial of the tokenizer that produced it (not
+// its address, which a later tokenizer may reuse); a colliding piece
+// replaces the slot's. Thread-local, so the threads of laya_tok_build_batch
 // need no lock.
-constexpr size_t PIECE_CACHE_BYTES = 64;
-constexpr size_t PIECE_CACHE_ENTRIES = 1 << 16;
+constexpr size_t PIECE_BYTES = 32, PIECE_IDS = 16, PIECE_SLOTS = 1 << 13;
 std::atomic<uint64_t> g_tok_serial{1};
 
+struct PieceSlot {
+    uint64_t owner;  // tokenizer serial, 0 = empty
+    uint32_t len, n_ids;
+    char bytes[PIECE_BYTES];
+    uint32_t ids[PIECE_IDS];
+};
+
 struct PieceCache {
-    uint64_t owner = 0;
-    std::unordered_map<std::string, std::vector<uint32_t>> map;
+    PieceSlot* slots = nullptr;
+    ~PieceCache() { free(slots); }
+    PieceSlot* slot(const char* p, size_t n) {
+        if (!slots) {
+            slots = static_cast<PieceSlot*>(calloc(PIECE_SLOTS, sizeof(PieceSlot)));
+            if (!slots) return nullptr;
+        }
+        uint64_t h = 1469598103934665603ull;  // FNV-1a
+        for (size_t i = 0; i < n; i++) h = (h ^ (uint8_t)p[i]) * 1099511628211ull;
+        return &slots[(h ^ (h >> 29)) & (PIECE_SLOTS - 1)];
+    }
 };
 thread_local PieceCache t_piece_cache;
 
@@ -475,20 +492,10 @@ thread_local PieceCache t_piece_cache;
 
 void laya_tok::bpe_piece(const char* p, size_t n, std::vector<uint32_t>& out) const {  // main.zig:2111-2156
     if (n == 0) return;
-    PieceCache* pc = nullptr;
-    std::string ckey;
-    if (n <= PIECE_CACHE_BYTES) {
-        pc = &t_piece_cache;
-        if (pc->owner != serial) {
-            pc->map.clear();
-            pc->owner = serial;
-        }
-        ckey.assign(p, n);
-        const auto it = pc->map.find(ckey);
-        if (it != pc->map.end()) {
-            out.insert(out.end(), it->second.begin(), it->second.end());
-            return;
-        }
+    PieceSlot* slot = n <= PIECE_BYTES ? t_piece_cache.slot(p, n) : nullptr;
+    if (slot && slot->owner == serial && slot->len == n && memcmp(slot->bytes, p, n) == 0) {
+        out.insert(out.end(), slot->ids, slot->ids + slot->n_ids);
+        return;
     }
     const size_t first_out = out.size();
     struct Sym {
@@ -501,27 +508,33 @@ void laya_tok::bpe_piece(const char* p, size_t n, std::vector<uint32_t>& out) co
         syms.push_back({(uint32_t)i, (uint32_t)(i + len)});
         i += len;
     }
+    // rank[s]: merge rank of the pair (s, s + 1), NONE if it is no merge.
+    // A merge changes only the two pairs beside it, so each merge costs two
+    // lookups and a scan of the ranks instead of a lookup per pair; the
+    // pair merged is the same (lowest rank, leftmost on ties).
+    constexpr uint32_t NONE = 0xFFFFFFFFu;
     char key[1024];
-    while (syms.size() > 1) {
-        uint32_t best = 0;
+    auto pair_rank = [&](size_t s) -> uint32_t {
+        const size_t la = syms[s].b - syms[s].a, lb = syms[s + 1].b - syms[s + 1].a;
+        if (la + lb + 1 > sizeof key) return NONE;
+        memcpy(key, p + syms[s].a, la);
+        key[la] = 0;
+        memcpy(key + la + 1, p + syms[s + 1].a, lb);
+        uint32_t r;
+        return merges.get(key, la + lb + 1, &r) ? r : NONE;
+    };
+    std::vector<uint32_t> rank(syms.size() - 1);
+    for (size_t s = 0; s < rank.size(); s++) rank[s] = pair_rank(s);
+    while (!rank.empty()) {
         size_t bi = 0;
-        bool found = false;
-        for (size_t s = 0; s + 1 < syms.size(); s++) {
-            const size_t la = syms[s].b - syms[s].a, lb = syms[s + 1].b - syms[s + 1].a;
-            if (la + lb + 1 > sizeof key) continue;
-            memcpy(key, p + syms[s].a, la);
-            key[la] = 0;
-            memcpy(key + la + 1, p + syms[s + 1].a, lb);
-            uint32_t r;
-            if (merges.get(key, la + lb + 1, &r) && (!found || r < best)) {
-                best = r;
-                bi = s;
-                found = true;
-            }
-        }
-        if (!found) break;
+        for (size_t s = 1; s < rank.size(); s++)
+            if (rank[s] < rank[bi]) bi = s;
+        if (rank[bi] == NONE) break;
         syms[bi].b = syms[bi + 1].b;
         syms.erase(syms.begin() + (long)bi + 1);
+        rank.erase(rank.begin() + (long)bi);  // the old pair (bi + 1, bi + 2) is now (bi, bi + 1)
+        if (bi < rank.size()) rank[bi] = pair_rank(bi);
+        if (bi > 0) rank[bi - 1] = pair_rank(bi - 1);
     }
     for (const Sym& s : syms) {
         uint32_t id;
@@ -531,9 +544,13 @@ void laya_tok::bpe_piece(const char* p, size_t n, std::vector<uint32_t>& out) co
             for (uint32_t i = s.a; i < s.b; i++) out.push_back(byte_ids[(uint8_t)p[i]]);
         }
     }
-    if (pc) {
-        if (pc->map.size() >= PIECE_CACHE_ENTRIES) pc->map.clear();
-        pc->map.emplace(std::move(ckey), std::vector<uint32_t>(out.begin() + (long)first_out, out.end()));
+    const size_t n_ids = out.size() - first_out;
+    if (slot && n_ids <= PIECE_IDS) {
+        slot->owner = serial;
+        slot->len = (uint32_t)n;
+        slot->n_ids = (uint32_t)n_ids;
+        memcpy(slot->bytes, p, n);
+        std::copy(out.begin() + (long)first_out, out.end(), slot->ids);
     }
 }
 
