@@ -98,6 +98,57 @@ class _Marshalled:
                                     ctypes.cast(oarr, ctypes.POINTER(ctypes.c_char_p)) if oarr else None, len(ob))
 
 
+class _Packed:
+    """The laya_decision array for many decisions, built with a few C-level
+    operations instead of one ctypes object per string: every string
+    NUL-terminated in one buffer, the pointers computed from its NUL
+    positions into a numpy array laid out as the C struct. A string that
+    holds a NUL itself (which the C side would cut there anyway) makes
+    `ok` false; the caller then uses _Marshalled."""
+
+    _dtype = np.dtype({"names": ["state", "qtype_name", "ins", "opts", "n_opts"],
+                       "formats": [np.uint64, np.uint64, np.uint64, np.uint64, np.uint32],
+                       "offsets": [_Decision.state.offset, _Decision.qtype_name.offset, _Decision.ins.offset,
+                                   _Decision.opts.offset, _Decision.n_opts.offset],
+                       "itemsize": ctypes.sizeof(_Decision)})
+
+    def __init__(self, decisions: Sequence):
+        self.n = n = len(decisions)
+        self.ok = False
+        strs: List = []
+        n_opts = np.empty(n, np.int64)
+        for i, (state, qn, ins, opts) in enumerate(decisions):
+            strs += (state, qn, ins)
+            strs += opts
+            n_opts[i] = len(opts)
+        if all(isinstance(x, str) for x in strs):
+            buf = ("\0".join(strs) + "\0").encode()
+        else:
+            buf = b"\0".join(_b(x) for x in strs) + b"\0"
+        self._buf = np.frombuffer(buf, dtype=np.uint8).copy()
+        ends = np.flatnonzero(self._buf == 0)
+        if len(ends) != len(strs):
+            return
+        base = np.uint64(self._buf.ctypes.data)
+        starts = np.concatenate([[0], ends[:-1] + 1]).astype(np.uint64) + base
+        first = np.concatenate([[0], np.cumsum(3 + n_opts)[:-1]]).astype(np.int64)
+        is_opt = np.ones(len(strs), dtype=bool)
+        is_opt[first] = is_opt[first + 1] = is_opt[first + 2] = False
+        self._opt_ptrs = np.ascontiguousarray(starts[is_opt], dtype=np.uint64)
+        opt_first = np.concatenate([[0], np.cumsum(n_opts)[:-1]]).astype(np.uint64)
+        self.arr = np.zeros(max(1, n), dtype=self._dtype)
+        self.arr["state"][:n] = starts[first]
+        self.arr["qtype_name"][:n] = starts[first + 1]
+        self.arr["ins"][:n] = starts[first + 2]
+        opts_ptr = np.uint64(self._opt_ptrs.ctypes.data) + opt_first * np.uint64(8)
+        self.arr["opts"][:n] = np.where(n_opts > 0, opts_ptr, np.uint64(0))
+        self.arr["n_opts"][:n] = n_opts
+        self.ok = True
+
+    def ptr(self):
+        return self.arr.ctypes.data_as(ctypes.POINTER(_Decision))
+
+
 class Tokenizer:
     def __init__(self, path: str):
         h = ctypes.c_void_p()
@@ -147,7 +198,10 @@ class Tokenizer:
                     head_max_len: int = HEAD_MAX_LEN) -> Dict[str, np.ndarray]:
         """decisions: (state, qtype_name, ins, opts) tuples. Returns the packed
         arrays ids, cu_seqlens, markers, cu_markers, qtypes."""
-        m = _Marshalled(decisions)
+        m = _Packed(decisions)
+        if not m.ok:
+            m = _Marshalled(decisions)
+        arr = m.ptr() if isinstance(m, _Packed) else m.arr
         n = m.n
         ids_cap = n * max_len
         mk_cap = sum(len(d[3]) for d in decisions)
@@ -157,7 +211,7 @@ class Tokenizer:
         cum = np.zeros(n + 1, np.int32)
         qt = np.zeros(max(1, n), np.uint32)
         nt, nm = ctypes.c_size_t(), ctypes.c_size_t()
-        _check(lib.laya_tok_build_batch(self._h, m.arr, n, max_len, head_max_len, threads, ids.ctypes.data, ids_cap,
+        _check(lib.laya_tok_build_batch(self._h, arr, n, max_len, head_max_len, threads, ids.ctypes.data, ids_cap,
                                         cu.ctypes.data, markers.ctypes.data, mk_cap, cum.ctypes.data, qt.ctypes.data,
                                         ctypes.byref(nt), ctypes.byref(nm)))
         return {"ids": ids[:nt.value].copy(), "cu_seqlens": cu, "markers": markers[:nm.value].copy(),

@@ -264,3 +264,25 @@ def test_piece_cache_is_per_tokenizer(tmp_path):
         assert ta2.encode(s) == oa.encode(s), s
     tc.close()
     ta2.close()
+
+
+@needs_vocab
+def test_build_batch_packing_paths(tok):
+    """build_batch lays the decision strings out in one buffer; bytes and
+    str inputs mixed, decisions without options, and a string holding a NUL
+    (the C side reads it up to the NUL, on the fallback path too) all pack
+    exactly as single builds do."""
+    from laya_zig_b200 import gpu
+    ds = [("state one two", "choice", "pick <mask>", ["a", "b"]),
+          (b"byte state", b"score", "ins <mask>", [b"x", "y", "z"]),
+          ("no options here", "noul", "ins", []),
+          ("tail state", "choice", "q <mask>", ["only"])]
+    ref = gpu.pack([tok.build(*d) for d in ds])
+    p = tok.build_batch(ds, threads=2)
+    for k in ("ids", "cu_seqlens", "cu_markers", "qtypes"):
+        np.testing.assert_array_equal(p[k], ref[k], err_msg=k)
+    cut = [("state\x00hidden", "choice", "pick <mask>", ["a", "b\x00c"]), ds[0]]
+    p = tok.build_batch(cut, threads=1)
+    want = gpu.pack([tok.build("state", "choice", "pick <mask>", ["a", "b"]), tok.build(*ds[0])])
+    for k in ("ids", "cu_seqlens", "cu_markers", "qtypes"):
+        np.testing.assert_array_equal(p[k], want[k], err_msg=k)
