@@ -14,6 +14,17 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) and the built CUDA library")
 
 
+def pytest_sessionstart(session):
+    """On a fresh checkout liblaya_gpu.so (kept out of git) is not there yet
+    and the package refuses to import without it; build it once, in-tree,
+    before any test imports the package (nvcc cross-compiles sm_100a on a
+    host without a GPU)."""
+    import subprocess
+    lib = os.path.join(ROOT, "laya_zig_b200", "liblaya_gpu.so")
+    if not os.path.exists(lib):
+        subprocess.run([sys.executable, "-m", "laya_zig_b200.build"], cwd=ROOT, check=True)
+
+
 @pytest.fixture(scope="session")
 def weights():
     from laya_zig_b200 import synth
