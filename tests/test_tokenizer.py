@@ -286,3 +286,34 @@ def test_build_batch_packing_paths(tok):
     want = gpu.pack([tok.build("state", "choice", "pick <mask>", ["a", "b"]), tok.build(*ds[0])])
     for k in ("ids", "cu_seqlens", "cu_markers", "qtypes"):
         np.testing.assert_array_equal(p[k], want[k], err_msg=k)
+
+
+@needs_vocab
+def test_concurrent_callers_get_sequential_results(tok, otok):
+    """A loaded tokenizer may be used from any number of threads (the BPE
+    cache is per thread): four Python threads encoding and building at once
+    (ctypes releases the GIL during the calls) get what one thread gets."""
+    import threading
+    texts = _random_texts(otok, 120, seed=23)
+    decs = _random_decisions(otok, 40, seed=29)
+    want_enc = [tok.encode(t) for t in texts]
+    want_b = tok.build_batch(decs, threads=1)
+    errors = []
+
+    def worker(k):
+        try:
+            for r in range(3):
+                for i in range(k, len(texts), 4):
+                    assert tok.encode(texts[i]) == want_enc[i]
+                got = tok.build_batch(decs, threads=1 + (k + r) % 3)
+                for key in ("ids", "cu_seqlens", "markers", "cu_markers", "qtypes"):
+                    np.testing.assert_array_equal(got[key], want_b[key])
+        except Exception as e:  # reported on the main thread
+            errors.append(repr(e))
+
+    ths = [threading.Thread(target=worker, args=(k,)) for k in range(4)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    assert not errors, errors[:3]
