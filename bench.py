@@ -14,6 +14,21 @@ batch of 64 decisions per step (weak scaling, model replicated, no
 collective on the data path); the time is the max over ranks of the summed
 per-step CUDA-event durations. `--impl reference` times the CPU path (the
 oracle's restatement of laya-zig's forward) on the host cores instead.
+
+Other workloads (not the headline line):
+  --workload sweep   65,536 decisions of 128-512 tokens in length buckets (strong scaling)
+  --workload gemm    the four projection shapes at M = 180 and M = 11,520, each
+                     launch timed alone (the reference's --benchgemm)
+  --workload long    one 8,192-token decision (latency, attention roofline)
+
+Kernel times in the rooflines: a CUDA graph of one forward with an event pair
+around every launch gives each launch's time; the event nodes stop
+programmatic dependent launch from overlapping neighbours, so those times
+over-count. The roofline time of a kernel family is its share of the
+profiled total applied to the real (PDL-overlapped) step time measured in
+the timed region; the raw event-pair figure is reported beside it. Peaks:
+MEASURED_PEAKS.json, burst bf16 for a run whose clocks saw no power cap,
+sustained bf16 when `sw_power_cap` was active.
 """
 from __future__ import annotations
 
@@ -70,6 +85,47 @@ def peaks():
         with open(p) as f:
             return json.load(f), "measured"
     return FALLBACK, "fallback"
+
+
+def tensor_peak(clk):
+    """(bf16 TFLOP/s peak, label): the burst figure unless the timed region
+    ran under the power cap, which only seconds-long loads reach."""
+    pk, src = peaks()
+    name = "MEASURED_PEAKS.json" if src == "measured" else "fallback"
+    capped = "sw_power_cap" in (clk or {}).get("reasons", [])
+    key = "bf16_tflops_sustained" if capped else "bf16_tflops"
+    why = "sw_power_cap active in the timed region" if capped else "no power cap in the timed region"
+    return float(pk.get(key, FALLBACK[key])), "%s %s (%s, %s)" % (name, key, src, why)
+
+
+def hbm_peak():
+    pk, src = peaks()
+    name = "MEASURED_PEAKS.json" if src == "measured" else "fallback"
+    return float(pk.get("hbm_gbs", FALLBACK["hbm_gbs"])), "%s hbm_gbs (%s)" % (name, src)
+
+
+def attn_flops_split(L: int):
+    """(global, sliding) attention FLOPs of one sequence: 4*768*L^2 per global
+    layer (8 encoder + 2 head), 4*768*S(L) per sliding layer (14)."""
+    s = sum(min(L, i + 65) - max(0, i - 64) for i in range(L))
+    return 4.0 * 768 * 10 * L * L, 4.0 * 768 * 14 * s
+
+
+def launch_profile(model, db, lg_ptr, act_ptr, stream, iters=5):
+    """Per-launch event-pair times of one forward, grouped: returns
+    (total_ms, {family: [ms per launch, ...]}) with the encoder attention
+    launches split into global (layer % 3 == 0, and the two head layers) and
+    sliding ones."""
+    prof = model.profile_launches(db, lg_ptr, act_ptr, iters=iters, stream=stream)
+    fam = {}
+    attn_i = 0
+    for stage, ms in prof:
+        key = stage
+        if stage == "attention":
+            key = "attention_global" if (attn_i >= 22 or attn_i % 3 == 0) else "attention_sliding"
+            attn_i += 1
+        fam.setdefault(key, []).append(ms / iters)
+    return sum(ms for _, ms in prof) / iters, fam
 
 
 def traffic_per_launch():
@@ -284,6 +340,176 @@ def run_sweep(args, world: int):
     }), flush=True)
 
 
+def _clock_region(local):
+    import torch
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    return Clocks([uuid] if uuid else [])
+
+
+GEMM_SHAPES = [("QKV", 2304, 768), ("attn-out", 768, 768), ("GLU Wi", 2304, 768), ("FFN-out", 768, 1152)]
+
+
+def run_gemm(args):
+    """--workload gemm: the projection shapes at M = 180 and 11,520 through
+    laya_gpu_linear (the drop-in for linear16: bf16 operands, f32 out,
+    tcgen05 cta_group::2 kernel), each launch timed alone with CUDA events on
+    its stream after an L2 flush; A ~ N(0, 1), W ~ N(0, 0.02), rounded to
+    bf16. Beside it, cuBLAS through torch.mm on the same operands (f32 out
+    where torch offers it). Every output is checked against an f64 product."""
+    import torch
+    from laya_zig_b200 import gpu
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+    flush = torch.empty(flush_bytes(), dtype=torch.uint8, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    steps, warm = max(args.steps, 1), max(args.warmup, 3)
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in ev:
+            flush.zero_()
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+    clocks = _clock_region(0)
+    clocks.start()
+    rows = []
+    for M in (180, 11520):
+        for name, N, K in GEMM_SHAPES:
+            a = torch.randn(M, K, device="cuda", generator=gen).to(torch.bfloat16)
+            w = (torch.randn(N, K, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+            out = torch.empty(M, N, dtype=torch.float32, device="cuda")
+            run = lambda: gpu.linear(a.data_ptr(), w.data_ptr(), 0, out.data_ptr(), M, N, K, "BF16", sp)
+            ms = timed(run)
+            ref = a.double() @ w.double().t()
+            err = float(((out.double() - ref).abs().amax(1) / ref.abs().amax(1)).max())
+            try:
+                cub = lambda: torch.mm(a, w.t(), out_dtype=torch.float32)
+                cub()
+                cub_kind = "torch.mm bf16 -> f32"
+            except Exception:
+                cub = lambda: torch.mm(a, w.t())
+                cub_kind = "torch.mm bf16 -> bf16"
+            cms = timed(cub)
+            fl = 2.0 * M * N * K
+            rows.append({"shape": name, "M": M, "N": N, "K": K, "us": ms * 1e3, "tflops": fl / (ms / 1e3) / 1e12,
+                         "cublas_us": cms * 1e3, "cublas_tflops": fl / (cms / 1e3) / 1e12, "cublas": cub_kind,
+                         "max_row_rel_err_vs_f64": err})
+            assert err < 1e-4, (name, M, err)
+    clk = clocks.stop()
+    peak, peak_src = tensor_peak(clk)
+    big = [r for r in rows if r["M"] == 11520]
+    fl = sum(2.0 * r["M"] * r["N"] * r["K"] for r in big)
+    t = sum(r["us"] for r in big) / 1e6
+    for r in rows:
+        r["frac"] = r["tflops"] / peak
+    print(json.dumps({
+        "metric": "projection GEMM TFLOP/s at M=11520 (QKV, attn-out, GLU Wi, FFN-out), each launch alone",
+        "value": fl / t / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps, "warmup": warm,
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (A ~ N(0,1), W ~ N(0,0.02), bf16)",
+        "config": {"workload": "isolated projection GEMMs through laya_gpu_linear (f32 out), M in {180, 11520}",
+                   "l2": "flushed before every timed launch (%d MB write)" % (flush_bytes() // 10**6),
+                   "time": "median of %d launches" % steps},
+        "roofline": {"bound": "tensor", "achieved": fl / t / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": fl / t / 1e12 / peak, "traffic": None, "peak_source": peak_src,
+                     "kernel": "gemm_pair_kernel<EPI_F32> (laya_gpu_linear)"},
+        "shapes": rows, "clocks": clk, "gpu_launches": len(rows) * (steps + warm),
+    }), flush=True)
+
+
+def run_long(args):
+    """--workload long: one 8,192-token decision with 16 markers (global
+    attention every third layer), resident in HBM; a step is one forward,
+    timed with CUDA events on its stream after an L2 flush. e2e: the host
+    call laya_gpu_forward with host ids. Attention and GEMM rooflines from the
+    per-launch profile (launches of milliseconds, so the event pairs cost
+    little)."""
+    import numpy as np
+    import torch
+    from laya_zig_b200 import gpu, synth
+    torch.cuda.set_device(0)
+    weights = synth.make_weights(0)
+    model = gpu.LayaGPU.from_bf16(weights, device=0, precision=args.precision)
+    d = synth.long_decision(8192, 16, seed=3)
+    p = gpu.pack([d])
+    dev = {k: torch.from_numpy(v.view(np.int32)).cuda() for k, v in p.items() if k != "max_len"}
+    M, G = len(p["ids"]), int(p["cu_markers"][-1])
+    db = gpu.DeviceBatch(dev["ids"].data_ptr(), dev["cu_seqlens"].data_ptr(), dev["markers"].data_ptr(),
+                         dev["cu_markers"].data_ptr(), dev["qtypes"].data_ptr(), 1, M, G, p["max_len"])
+    logits = torch.zeros(G, dtype=torch.float32, device="cuda")
+    act = torch.zeros((1, 2), dtype=torch.float32, device="cuda")
+    flush = torch.empty(flush_bytes(), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+    steps = max(args.steps, 1)
+    for _ in range(max(3, args.warmup)):
+        model.forward_device(db, logits.data_ptr(), act.data_ptr(), stream=sp)
+    model.sync()
+    clocks = _clock_region(0)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        flush.zero_()
+        a.record(stream)
+        model.forward_device(db, logits.data_ptr(), act.data_ptr(), stream=sp)
+        b.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    model.sync()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        model.forward(d.ids, d.qtype, d.markers)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / steps
+    prof_total, fam = launch_profile(model, db, logits.data_ptr(), act.data_ptr(), sp, iters=3)
+    attr = ms / prof_total
+    peak, peak_src = tensor_peak(clk)
+    g_fl, s_fl = attn_flops_split(M)
+    gemm_fl = 2.0 * M * GEMM_PARAMS
+    fams = {"attention_global": g_fl, "attention_sliding": s_fl,
+            "projection GEMMs": gemm_fl}
+    gemm_ms = sum(sum(fam.get(f, [])) for f in ["gemm_qkv", "gemm_out", "gemm_up", "gemm_down"])
+    times = {"attention_global": sum(fam.get("attention_global", [])),
+             "attention_sliding": sum(fam.get("attention_sliding", [])), "projection GEMMs": gemm_ms}
+    rl = [{"kernel": k, "bound": "tensor", "algorithmic_flops": fl, "event_pair_ms": times[k],
+           "achieved": fl / (times[k] * attr / 1e3) / 1e12, "achieved_event_pairs": fl / (times[k] / 1e3) / 1e12,
+           "peak": peak, "unit": "TFLOP/s", "frac": fl / (times[k] * attr / 1e3) / 1e12 / peak,
+           "peak_source": peak_src} for k, fl in fams.items() if times[k] > 0]
+    a = act.cpu().numpy()
+    assert np.isfinite(a).all() and abs(a.sum() - 1) < 1e-4
+    h2d = 4 * M + 4 * 2 + 4 + 4 * G + 4 * 2
+    print(json.dumps({
+        "metric": "long-context decision latency (1 x 8192 tokens, 16 markers)", "value": 1e3 / ms,
+        "unit": "decisions/s", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": args.precision,
+        "data": "synthetic (seeded weights and token ids)",
+        "config": {"workload": "one decision of 8192 tokens, 16 markers at random positions, global attention "
+                               "every third layer, sliding window 128 elsewhere",
+                   "l2": "flushed between timed steps"},
+        "latency_ms": ms, "roofline": rl[0] if rl else None, "rooflines": rl,
+        "whole_step_tflops": (g_fl + s_fl + gemm_fl) / (ms / 1e3) / 1e12,
+        "e2e": {"value": 1e3 / e2e_ms, "unit": "decisions/s", "latency_ms": e2e_ms, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 4 * G + 8 + 4 + 768 * 4},
+        "timing": "family share of the per-launch event-pair profile x the timed step (profiled %.3f ms vs %.3f ms)"
+                  % (prof_total, ms),
+        "clocks": clk, "gpu_launches": (sum(len(v) for v in fam.values()) + 2) * steps,
+    }), flush=True)
+    model.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -292,8 +518,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="snake", choices=["snake", "sweep"],
-                    help="snake: the 64 x 180 headline batch (default); sweep: the bucketed throughput sweep")
+    ap.add_argument("--workload", default="snake", choices=["snake", "sweep", "gemm", "long"],
+                    help="snake: the 64 x 180 headline batch (default); sweep: the bucketed throughput sweep; "
+                         "gemm: isolated projection GEMMs; long: one 8192-token decision")
     ap.add_argument("--sweep-n", type=int, default=65536)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -302,6 +529,12 @@ def main():
         return
     if args.workload == "sweep":
         run_sweep(args, world)
+        return
+    if args.workload == "gemm":
+        run_gemm(args)
+        return
+    if args.workload == "long":
+        run_long(args)
         return
 
     import numpy as np
@@ -386,45 +619,58 @@ def main():
     h2d = 4 * M + 4 * (S + 1) + 4 * S + 4 * G + 4 * (S + 1)
     d2h = 4 * G + 8 * S + 4
 
-    # dominant kernel (projection GEMMs): CUDA events around every launch, same stream
-    stage_ms, launches = model.profile(db, logits.data_ptr(), act.data_ptr(), iters=5, stream=sp)
-    gemm_stages = ["gemm_qkv", "gemm_out", "gemm_up", "gemm_down"]
-    gemm_ms = sum(stage_ms[s] for s in gemm_stages) / 5
-    gemm_launches = sum(launches[s] for s in gemm_stages)
+    # Kernel families: per-launch event-pair times of one forward (5 passes),
+    # attributed to the real step by their share of the profiled total.
+    step_ms = t_max / args.steps
+    prof_total, fam = launch_profile(model, db, logits.data_ptr(), act.data_ptr(), sp, iters=5)
+    attr = step_ms / prof_total
+    gemm_fams = ["gemm_qkv", "gemm_out", "gemm_up", "gemm_down"]
+    gemm_prof_ms = sum(sum(fam.get(f, [])) for f in gemm_fams)
+    gemm_launches = sum(len(fam.get(f, [])) for f in gemm_fams)
     gemm_flops = 2.0 * M * GEMM_PARAMS
-    pk, src = peaks()
-    peak = float(pk.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"]))
-    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
+    peak, peak_src = tensor_peak(clk)
+    achieved = gemm_flops / (gemm_prof_ms * attr / 1e3) / 1e12
+    achieved_pairs = gemm_flops / (gemm_prof_ms / 1e3) / 1e12
     tr = traffic_per_launch()
-    attn_step = sum(attn_flops(len(d.ids)) for d in batch)
-    flops_step = gemm_flops + attn_step
-    # the other kernel families against their own bounds, same profiled pass
-    hbm = float(pk.get("hbm_gbs", FALLBACK["hbm_gbs"]))
-    hbm_src = "%s hbm_gbs (%s)" % ("MEASURED_PEAKS.json" if src == "measured" else "fallback", src)
-
-    def per_launch_ms(stage):
-        return stage_ms[stage] / 5 / max(1, launches[stage])
+    attn_g = sum(attn_flops_split(len(d.ids))[0] for d in batch)
+    attn_s = sum(attn_flops_split(len(d.ids))[1] for d in batch)
+    flops_step = gemm_flops + attn_g + attn_s
+    hbm, hbm_src = hbm_peak()
+    timing = ("family share of a per-launch event-pair profile (5 passes) x the timed step time; "
+              "profiled total %.3f ms vs step %.3f ms" % (prof_total, step_ms))
 
     secondary = []
-    if launches.get("norm"):
-        ln_bytes = M * (D_MODEL * 4 + D_MODEL * 2)  # f32 row in, 16-bit row out
-        a = ln_bytes / (per_launch_ms("norm") / 1e3) / 1e9
-        secondary.append({"kernel": "ln_kernel (%d launches per step)" % launches["norm"], "bound": "hbm",
-                          "algorithmic_bytes_per_launch": ln_bytes, "achieved": a, "peak": hbm, "unit": "GB/s",
-                          "frac": a / hbm, "peak_source": hbm_src})
-    if launches.get("attention"):
-        a = attn_step / (stage_ms["attention"] / 5 / 1e3) / 1e12
-        secondary.append({"kernel": "attention_kernel (%d launches per step)" % launches["attention"],
-                          "bound": "tensor", "algorithmic_flops_per_step": attn_step, "achieved": a, "peak": peak,
-                          "unit": "TFLOP/s", "frac": a / peak,
-                          "peak_source": "%s bf16_tflops_sustained (%s)" % (
-                              "MEASURED_PEAKS.json" if src == "measured" else "fallback", src)})
-    for st, name, nbytes in (("embed", "embed_kernel", M * (D_MODEL * 2 + D_MODEL * 4 + D_MODEL * 2)),
-                             ("final", "final_kernel", M * (D_MODEL * 4 + D_MODEL * 4 + D_MODEL * 2))):
-        if launches.get(st):
-            a = nbytes / (per_launch_ms(st) / 1e3) / 1e9
-            secondary.append({"kernel": name, "bound": "hbm", "algorithmic_bytes_per_launch": nbytes, "achieved": a,
-                              "peak": hbm, "unit": "GB/s", "frac": a / hbm, "peak_source": hbm_src})
+    for f, name, nbytes in (("norm", "ln_kernel", M * (D_MODEL * 4 + D_MODEL * 2)),
+                            ("embed", "embed_kernel", M * (D_MODEL * 2 + D_MODEL * 4 + D_MODEL * 2 + 256)),
+                            ("final", "final_kernel", M * (D_MODEL * 4 + D_MODEL * 4 + D_MODEL * 2))):
+        if fam.get(f):
+            per = sum(fam[f]) / len(fam[f])
+            a = nbytes / (per * attr / 1e3) / 1e9
+            secondary.append({"kernel": "%s (%d launches per step)" % (name, len(fam[f])), "bound": "hbm",
+                              "algorithmic_bytes_per_launch": nbytes, "achieved": a, "peak": hbm, "unit": "GB/s",
+                              "frac": a / hbm, "achieved_event_pairs": nbytes / (per / 1e3) / 1e9,
+                              "peak_source": hbm_src})
+    for f, fl in (("attention_sliding", attn_s), ("attention_global", attn_g)):
+        if fam.get(f):
+            t = sum(fam[f])
+            a = fl / (t * attr / 1e3) / 1e12
+            secondary.append({"kernel": "attention_kernel, %s layers (%d launches per step)" % (f[10:], len(fam[f])),
+                              "bound": "tensor", "algorithmic_flops_per_step": fl, "achieved": a, "peak": peak,
+                              "unit": "TFLOP/s", "frac": a / peak, "achieved_event_pairs": fl / (t / 1e3) / 1e12,
+                              "peak_source": peak_src})
+    for f in gemm_fams:
+        if fam.get(f):
+            per_tok = {"gemm_qkv": (22 * 3 * 768 * 768 + 2 * 3 * 768 * 768),
+                       "gemm_out": 24 * 768 * 768,
+                       "gemm_up": 22 * 2 * 1152 * 768 + 2 * 3072 * 768,
+                       "gemm_down": 22 * 1152 * 768 + 2 * 3072 * 768}[f]
+            fl = 2.0 * M * per_tok
+            t = sum(fam[f])
+            a = fl / (t * attr / 1e3) / 1e12
+            secondary.append({"kernel": "gemm_pair_kernel %s (%d launches per step)" % (f, len(fam[f])),
+                              "bound": "tensor", "algorithmic_flops_per_step": fl, "achieved": a, "peak": peak,
+                              "unit": "TFLOP/s", "frac": a / peak, "achieved_event_pairs": fl / (t / 1e3) / 1e12,
+                              "peak_source": peak_src})
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -443,15 +689,14 @@ def main():
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": tr,
                      "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 projection GEMMs, %d launches per step)" % gemm_launches,
-                     "peak_source": "%s bf16_tflops_sustained (%s)" % ("MEASURED_PEAKS.json" if src == "measured"
-                                                                        else "fallback", src),
+                     "peak_source": peak_src, "timing": timing, "achieved_event_pairs": achieved_pairs,
                      "algorithmic_flops_per_step": gemm_flops},
         "cpu_baseline": base,
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": sum(launches.values()) * args.steps,
+        "gpu_launches": (sum(len(v) for v in fam.values()) + (2 if G else 0)) * args.steps,
         "clocks": clk,
-        "stage_ms_per_step": {k: v / 5 for k, v in stage_ms.items()},
-        "whole_step_tflops": flops_step / (t_max / args.steps / 1e3) / 1e12,
+        "family_ms_per_step": {k: sum(v) * attr for k, v in fam.items()},
+        "whole_step_tflops": flops_step / (step_ms / 1e3) / 1e12,
         "secondary_rooflines": secondary,
     }
     print(json.dumps(out), flush=True)

@@ -16,6 +16,7 @@
  *                            act, pooled: main.zig:2529-2541; hidden state
  *                            left in f.s.x, main.zig:2266-2294)
  *   laya_gpu_forward_trace   --dumpstats          src/main.zig:113-121, 2651-2777
+ *   laya_gpu_forward_dumpstats  (the same, as the reference's [dump] text)
  *   laya_gpu_linear          linear16             src/main.zig:1088-1099
  *                            (checked by --selftest, main.zig:420-536)
  *
@@ -133,8 +134,14 @@ LAYA_API int laya_gpu_forward_batch(laya_ctx* ctx, const laya_seq* seqs, uint32_
  * pointers (pooled, hidden nullable). Asynchronous on `stream`, a
  * cudaStream_t of the context's device (NULL = the legacy default stream,
  * as everywhere in CUDA); call laya_gpu_sync to wait and to collect
- * device-side errors. Inputs are not validated on the host:
- * bad ids or markers are clamped and reported by laya_gpu_sync. */
+ * device-side errors. Inputs are not validated on the host; the kernels
+ * check what they read: an id >= LAYA_VOCAB, a marker outside its sequence,
+ * a qtype > 2, offset tables that are not runs of [0, n_tokens) and
+ * [0, n_markers) in order (cu_seqlens[0] = cu_markers[0] = 0,
+ * cu_seqlens[n_seqs] = n_tokens, cu_markers[n_seqs] = n_markers), a
+ * sequence longer than max_len or with more than LAYA_MAX_MARKERS markers.
+ * Such an input is clamped or skipped without any access outside the
+ * buffers, and laya_gpu_sync returns LAYA_ERR_ARG. */
 LAYA_API int laya_gpu_forward_device(laya_ctx* ctx, const laya_batch* batch, float* logits, float* act, float* pooled,
                             float* hidden, void* stream);
 
@@ -146,6 +153,28 @@ LAYA_API int laya_gpu_sync(laya_ctx* ctx);
  * l0..l21, final, temb, h0, h1. */
 LAYA_API int laya_gpu_forward_trace(laya_ctx* ctx, const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers,
                            uint32_t K, float* logits, float* act, float* trace);
+
+/* --dumpstats (src/main.zig:113-130, 2651-2777): forward() of one sequence
+ * plus the text the reference prints for it, NUL-terminated, in its line
+ * formats: "[dump] meta L=.. qtype=..", the ids eight per "[dump] ids" line,
+ * one "[dump] <tag> x0 x1 x2 sum asum" line per tag (emb, l0..l21, final,
+ * temb, h0, h1; the first three values of the hidden state and its sum and
+ * absolute sum in f64, computed on the device), then "[dump] mark" and
+ * "[dump] logit". *text_len (nullable) receives the bytes the text needs,
+ * NUL included; if `cap` is smaller, nothing is written and LAYA_ERR_ARG is
+ * returned (the forward has run and logits/act are filled). */
+LAYA_API int laya_gpu_forward_dumpstats(laya_ctx* ctx, const uint32_t* ids, uint32_t L, uint32_t qtype,
+                                        const uint32_t* markers, uint32_t K, float* logits, float* act, char* text,
+                                        uint64_t cap, uint64_t* text_len);
+
+/* The text part of laya_gpu_forward_dumpstats, host only (no device, no
+ * context): stats[LAYA_TRACE_TAGS][5] = x[0], x[1], x[2], sum, absolute sum
+ * per tag, formatted with ids, markers and logits into the reference's
+ * `[dump]` lines (src/main.zig:113-130). Same `text`/`cap`/`text_len`
+ * contract; a failure is described by laya_gpu_last_error(NULL). */
+LAYA_API int laya_gpu_format_dump(const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers, uint32_t K,
+                                  const float* logits, const double* stats, char* text, uint64_t cap,
+                                  uint64_t* text_len);
 
 /* Finer than --dumpstats: every intermediate of encoder layer `layer`
  * (0..21) for one sequence, as the GPU holds it. 16-bit buffers are raw
@@ -183,6 +212,15 @@ typedef enum {
 LAYA_API int laya_gpu_forward_profile(laya_ctx* ctx, const laya_batch* batch, float* logits, float* act, int iters,
                                       void* stream, float* stage_ms, int* stage_launches);
 
+/* The same capture, per launch: launch_ms[i] receives the summed time of the
+ * forward's i-th timed launch (in launch order; the decision tail's three
+ * kernels count as one) over all iterations, launch_stage[i] its laya_stage.
+ * *n_launches (nullable) receives the count; at most `cap` are written.
+ * Synchronous. */
+LAYA_API int laya_gpu_forward_profile_launches(laya_ctx* ctx, const laya_batch* batch, float* logits, float* act,
+                                               int iters, void* stream, float* launch_ms, int* launch_stage, int cap,
+                                               int* n_launches);
+
 /* The decision tail alone (option scorer + act/escalate head) over final
  * hidden states the caller already holds in device memory, allocating
  * nothing. No counterpart in the reference: it is for callers that cannot
@@ -192,10 +230,16 @@ LAYA_API int laya_gpu_forward_profile(laya_ctx* ctx, const laya_batch* batch, fl
  * their workspace. Its scratch is a static device array sized for
  * LAYA_NOALLOC_MAX_MARKERS markers (6.4 MB, held by every GPU that loads
  * the library until exit); larger calls are rejected with LAYA_ERR_ARG.
- * hidden[n_tokens][768] f32, cu_seqlens/cu_markers[n_seqs + 1],
+ * hidden[cu_seqlens[n_seqs]][768] f32, cu_seqlens/cu_markers[n_seqs + 1],
  * markers[n_markers]; outputs logits[n_markers], act[2 * n_seqs],
- * pooled[n_seqs][768], all device pointers. Asynchronous on `stream` (NULL
- * = the legacy default stream); laya_gpu_sync reports device-side errors.
+ * pooled[n_seqs][768], all device pointers. As in laya_gpu_forward_device,
+ * each sequence holds at most LAYA_MAX_MARKERS (1024) markers, and the
+ * device-resident tables are checked by the kernels, not the host: a marker
+ * outside its sequence, a sequence with more than 1024 markers or offsets
+ * out of order (cu_markers[0] = 0, cu_markers[n_seqs] = n_markers) make
+ * laya_gpu_sync return LAYA_ERR_ARG, with nothing read or written outside
+ * the buffers. Asynchronous on `stream` (NULL = the legacy default stream);
+ * the caller's current device is left as it was.
  * The first call on a device resolves the array's device address
  * (cudaGetSymbolAddress, which may load the module): make it before any
  * stream capture. Calls share the array: calls that overlap on the GPU race. */

@@ -5,7 +5,9 @@
 Each .cu (nvcc) and .cpp (g++, host-only) under csrc/ compiles to an
 object in _build/ (in parallel, skipped when newer than its sources), then they link into laya_zig_b200/liblaya_gpu.so
 with the CUDA runtime linked statically, so the library loads on a host
-without a GPU (the driver is resolved at first use).
+without a GPU (the driver is resolved at first use). The plain C host
+program host/laya_forward.c is then built against it as
+laya_zig_b200/laya_forward.
 """
 from __future__ import annotations
 
@@ -61,6 +63,23 @@ def _compile(src: str, verbose_ptxas: bool, force: bool) -> str:
     return obj
 
 
+HOST_SRC = os.path.join(HERE, "host", "laya_forward.c")
+HOST_EXE = os.path.join(HERE, "laya_forward")
+
+
+def build_host(force: bool = False) -> str:
+    """The plain C host program (host/laya_forward.c) against the library."""
+    newest = max(os.path.getmtime(p) for p in [HOST_SRC, LIB] + glob.glob(os.path.join(ROOT, "include", "*.h")))
+    if force or not os.path.exists(HOST_EXE) or os.path.getmtime(HOST_EXE) < newest:
+        cmd = ["gcc", "-std=c99", "-O2", "-Wall", "-Wextra", "-Werror", "-D_DEFAULT_SOURCE", "-I",
+               os.path.join(ROOT, "include"), HOST_SRC, "-o", HOST_EXE, "-L", HERE, "-llaya_gpu",
+               "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("host program build failed:\n%s%s" % (r.stdout, r.stderr))
+    return HOST_EXE
+
+
 def build(verbose_ptxas: bool = False, force: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
@@ -71,6 +90,7 @@ def build(verbose_ptxas: bool = False, force: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s%s" % (r.stdout, r.stderr))
+    build_host(force)
     return LIB
 
 

@@ -108,7 +108,8 @@ __device__ __forceinline__ void load_tile(T* tile, const T* src, int ld, int r0,
 
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
-                                                            const int* __restrict__ cu_seqlens, int window) {
+                                                            const int* __restrict__ cu_seqlens, int M, int max_len,
+                                                            int window, int* err) {
     extern __shared__ __align__(128) uint8_t att_smem[];  // Q tile, then NST K tiles, then NST V tiles
     T* sQ = reinterpret_cast<T*>(att_smem);
     T* sK = sQ + QB * 64;
@@ -118,6 +119,13 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
     const int seq = blockIdx.z, h = blockIdx.y;
     const int start = cu_seqlens[seq];  // batch offsets: written before the forward starts
     const int L = cu_seqlens[seq + 1] - start;
+    // A device-resident offset table is not checked on the host: a sequence
+    // that is not a run of [0, M) no longer than max_len (the grid's extent)
+    // is flagged and left alone, so no row outside the batch is touched.
+    if (start < 0 || L < 0 || L > max_len || start > M - L) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_BAD_INDEX);
+        return;
+    }
     const int q0 = blockIdx.x * QB;
     if (q0 >= L) return;
     griddep_wait();  // qkv comes from the preceding projection
@@ -298,15 +306,16 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
 
 }  // namespace
 
-cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* cu_seqlens, int n_seqs, int max_len,
-                             int window, cudaStream_t stream) {
+cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* cu_seqlens, int n_seqs, int M,
+                             int max_len, int window, int* err, cudaStream_t stream) {
     if (n_seqs <= 0 || max_len <= 0) return cudaSuccess;
     dim3 grid((max_len + QB - 1) / QB, H, n_seqs);
     if (bf16)
         return launch_k(attention_kernel<__nv_bfloat16>, grid, THREADS, SMEM_BYTES, stream,
-                        static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, window);
+                        static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, M,
+                        max_len, window, err);
     return launch_k(attention_kernel<__half>, grid, THREADS, SMEM_BYTES, stream, static_cast<const __half*>(qkv),
-                    static_cast<__half*>(out), cu_seqlens, window);
+                    static_cast<__half*>(out), cu_seqlens, M, max_len, window, err);
 }
 
 cudaError_t attention_prepare() {

@@ -12,9 +12,15 @@ cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_se
                          int* seq_of, int* err, cudaStream_t s);
 cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const float* b, int M, int num_sms,
                       cudaStream_t s);
+// pre_temb (nullable): [M][768] f32, receives LN_final(x) before the type
+// embedding is added (the reference's "final" --dumpstats point).
 cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const float* type_emb,
                          const uint32_t* qtypes, const int* seq_of, const float* w1, const float* b1, int M,
-                         cudaStream_t s);
+                         float* pre_temb, int* err, cudaStream_t s);
+
+// out5 = {x[0], x[1], x[2], sum, absolute sum} of n f32 values, in f64
+// (the reference's --dumpstats fingerprint, src/main.zig:113-121).
+cudaError_t launch_dump_stats(const float* x, size_t n, double* out5, cudaStream_t s);
 
 // tail.cu ------------------------------------------------------------------
 struct TailWeights {
@@ -24,9 +30,14 @@ struct TailWeights {
 constexpr int SCORER_GROUPS = D / 64;  // partial sums per marker, one per 64 scorer outputs
 constexpr int MAX_MARKERS_PER_SEQ = 1024;
 
-// mv: [G][768] scratch, partial: [G][SCORER_GROUPS] scratch.
+// mv: [G][768] scratch, partial: [G][SCORER_GROUPS] scratch. x has M rows;
+// M < 0 takes cu_seqlens[n_seqs] as the row count. The offset tables are
+// checked on the device: a marker outside its sequence, a sequence's marker
+// run outside [0, G) or longer than MAX_MARKERS_PER_SEQ, or a [CLS] row
+// outside [0, M) sets ERR_BAD_INDEX and is skipped (its outputs zeroed or
+// left unwritten), so nothing outside the buffers is read or written.
 cudaError_t launch_tail(const float* x, const int* cu_seqlens, const uint32_t* markers, const int* cu_markers,
-                        int n_seqs, int G, const TailWeights& w, float* mv, float* partial, float* logits,
+                        int n_seqs, int G, int M, const TailWeights& w, float* mv, float* partial, float* logits,
                         float* act, float* pooled, int* err, cudaStream_t s);
 
 // convert.cu ---------------------------------------------------------------

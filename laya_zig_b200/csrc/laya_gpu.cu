@@ -97,6 +97,7 @@ struct laya_ctx {
     float* d_pooled = nullptr;
     int* d_err = nullptr;
     int* h_err = nullptr;  // pinned
+    double* d_stats = nullptr;  // [LAYA_TRACE_TAGS][5] --dumpstats fingerprints
     void* h_stage = nullptr;
     size_t h_stage_bytes = 0;
 
@@ -123,6 +124,20 @@ int fail(laya_ctx* c, int code, const char* fmt, ...) {
             return fail(c, e_ == cudaErrorMemoryAllocation ? LAYA_ERR_OOM : LAYA_ERR_CUDA, "%s: %s (%s:%d)", \
                         #call, cudaGetErrorString(e_), __FILE__, __LINE__);                           \
     } while (0)
+
+// Makes a context's device current for one entry point and gives the
+// caller's current device back on return, so a call never changes which
+// device the calling thread works on.
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t set(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        return cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
 
 size_t elem_size(int dt) { return dt == LAYA_DT_F32 ? 4 : 2; }
 
@@ -306,8 +321,8 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
         if (w.attn_norm) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.attn_norm, nullptr, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_QKV,
             gemm(c, EPI_QKV, am.a_xn, w.m_qkv, am.o_qkv, M, 3 * D, D, nullptr, 2 * D, s));
-        RUN(LAYA_STAGE_ATTN,
-            launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, (l % 3) ? WINDOW : -1, s));
+        RUN(LAYA_STAGE_ATTN, launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, M, b.maxlen,
+                                              (l % 3) ? WINDOW : -1, c->d_err, s));
         RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_wo, am.o_x, M, D, D, nullptr, 0, s));
         RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.mlp_norm, nullptr, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_UP,
@@ -315,14 +330,17 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
         RUN(LAYA_STAGE_GEMM_DOWN, gemm(c, EPI_RESID, am.a_mlp, w.m_wo2, am.o_x, M, D, INTER, nullptr, 0, s));
         hook.tap(1 + l);
     }
+    float* pre_temb = hook.pre_temb();
     RUN(LAYA_STAGE_FINAL, launch_final(c->bf16, c->x, c->xn, c->final_norm, c->type_emb, b.qt, c->seq_of,
-                                       c->head[0].n1w, c->head[0].n1b, M, s));
+                                       c->head[0].n1w, c->head[0].n1b, M, pre_temb, c->d_err, s));
+    hook.tap(23, pre_temb);
     hook.tap(24);
     for (int l = 0; l < HEAD_LAYERS; l++) {
         const HeadW& w = c->head[l];
         if (l > 0) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n1w, w.n1b, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_QKV, gemm(c, EPI_QKV, am.a_xn, w.m_in, am.o_qkv, M, 3 * D, D, w.in_b, 0, s));
-        RUN(LAYA_STAGE_ATTN, launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.maxlen, -1, s));
+        RUN(LAYA_STAGE_ATTN,
+            launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, M, b.maxlen, -1, c->d_err, s));
         RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_out, am.o_x, M, D, D, w.out_b, 0, s));
         RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n2w, w.n2b, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_UP,
@@ -331,8 +349,8 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
             gemm(c, EPI_RESID, am.a_ff, w.m_l2, am.o_x, M, D, HEAD_FF, w.l2_b, 0, s));
         hook.tap(25 + l);
     }
-    RUN(LAYA_STAGE_TAIL, launch_tail(c->x, b.cu, b.mk, b.cum, b.S, b.G, c->tail, c->mv, c->partial, o.logits, o.act,
-                                     o.pooled ? o.pooled : c->d_pooled, c->d_err, s));
+    RUN(LAYA_STAGE_TAIL, launch_tail(c->x, b.cu, b.mk, b.cum, b.S, b.G, M, c->tail, c->mv, c->partial, o.logits,
+                                     o.act, o.pooled ? o.pooled : c->d_pooled, c->d_err, s));
     hook.extra(LAYA_STAGE_TAIL, b.G > 0 ? 2 : 0);  // launch_tail issues 3 kernels when there are markers
     if (o.hidden) {
         e = cudaMemcpyAsync(o.hidden, c->x, (size_t)M * D * 4, cudaMemcpyDeviceToDevice, s);
@@ -345,11 +363,15 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
 struct NoHook {
     void begin(int) {}
     void end(int) {}
-    void tap(int) {}
+    void tap(int, const float* = nullptr) {}
     void extra(int, int) {}
+    float* pre_temb() { return nullptr; }
 };
 
-// Copies x to the host after every --dumpstats point.
+// Copies x to the host after every --dumpstats point. The "final" point
+// (the final LayerNorm before the type embedding) is written by the final
+// kernel into the qkv buffer, free between the last encoder layer and the
+// first head layer (M x 768 f32 fits in its M x 2304 16-bit elements).
 struct TraceHook {
     laya_ctx* c;
     float* trace;
@@ -357,7 +379,27 @@ struct TraceHook {
     void begin(int) {}
     void end(int) {}
     void extra(int, int) {}
-    void tap(int tag) { cudaMemcpyAsync(trace + (size_t)tag * LD, c->x, LD * 4, cudaMemcpyDeviceToHost, c->stream); }
+    float* pre_temb() { return reinterpret_cast<float*>(c->qkv); }
+    void tap(int tag, const float* src = nullptr) {
+        cudaMemcpyAsync(trace + (size_t)tag * LD, src ? src : c->x, LD * 4, cudaMemcpyDeviceToHost, c->stream);
+    }
+};
+
+// --dumpstats on the device: after every dump point, the first three values,
+// the sum and the absolute sum of the [M][768] state (f64), into
+// c->d_stats[tag][5].
+struct StatsHook {
+    laya_ctx* c;
+    size_t n;
+    cudaError_t err = cudaSuccess;
+    void begin(int) {}
+    void end(int) {}
+    void extra(int, int) {}
+    float* pre_temb() { return reinterpret_cast<float*>(c->qkv); }
+    void tap(int tag, const float* src = nullptr) {
+        const cudaError_t e = launch_dump_stats(src ? src : c->x, n, c->d_stats + (size_t)tag * 5, c->stream);
+        if (err == cudaSuccess) err = e;
+    }
 };
 
 // Copies every intermediate of one encoder layer to the host.
@@ -372,6 +414,7 @@ struct DumpHook {
     }
     void begin(int) {}
     void extra(int, int) {}
+    float* pre_temb() { return nullptr; }
     void end(int st) {
         if (cur != target) return;
         const size_t M16 = (size_t)M * 2;
@@ -387,7 +430,7 @@ struct DumpHook {
             default: break;
         }
     }
-    void tap(int tag) {
+    void tap(int tag, const float* = nullptr) {
         cur = tag;  // tag 0 follows the embedding, tag 1 + l follows layer l
         norms = 0;
         if (tag == 0 && target == 0) get(xn_attn, c->xn, (size_t)M * 2 * D);
@@ -424,13 +467,15 @@ struct ProfileHook {
         cudaEventRecordWithFlags(ev[used + 1], s, cudaEventRecordExternal);
         used += 2;
     }
-    void tap(int) {}
+    void tap(int, const float* = nullptr) {}
+    float* pre_temb() { return nullptr; }
     void extra(int st, int n) { launches[st] += n; }
-    void collect(float* stage_ms) const {
-        for (size_t i = 0; i < used; i += 2) {
+    // adds each timed launch's milliseconds to acc[launch]
+    void collect_each(std::vector<float>& acc) const {
+        for (size_t i = 0; i + 1 < used && i / 2 < acc.size(); i += 2) {
             float ms = 0.f;
             cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
-            stage_ms[stage[i / 2]] += ms;
+            acc[i / 2] += ms;
         }
     }
     ~ProfileHook() {
@@ -604,6 +649,8 @@ int create_impl(laya_ctx* c, const laya_tensor* t, int n) {
     CK(cudaMemsetAsync(c->d_err, 0, 4, c->stream));
     CK(cudaMallocHost(&c->h_err, 4));
     *c->h_err = 0;
+    CK(cudaMalloc(&c->d_stats, LAYA_TRACE_TAGS * 5 * sizeof(double)));
+    c->allocs.push_back(c->d_stats);
 
     // one device staging buffer, as large as the largest tensor given
     size_t stage_bytes = 0;
@@ -727,7 +774,8 @@ const char* laya_gpu_last_error(const laya_ctx* ctx) { return ctx ? ctx->err.c_s
 
 void laya_gpu_destroy(laya_ctx* c) {
     if (!c) return;
-    cudaSetDevice(c->device);
+    DeviceGuard dg;
+    dg.set(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     free_workspace(c);
     for (void* p : c->allocs) cudaFree(p);
@@ -746,6 +794,9 @@ int laya_gpu_create(int device, const laya_tensor* tensors, int n_tensors, int p
     const int ndev = laya_gpu_device_count();
     if (device < 0 || device >= ndev)
         return fail(nullptr, LAYA_ERR_NO_DEVICE, "device %d requested, %d visible", device, ndev);
+    DeviceGuard dg;  // create_impl makes `device` current
+    dg.prev = -1;
+    if (cudaGetDevice(&dg.prev) != cudaSuccess) dg.prev = -1;
     laya_ctx* c = new laya_ctx();
     c->device = device;
     c->bf16 = precision == LAYA_PREC_BF16;
@@ -764,7 +815,8 @@ int laya_gpu_forward_batch(laya_ctx* c, const laya_seq* seqs, uint32_t n, float*
     if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
     if (!seqs || n == 0) return fail(c, LAYA_ERR_ARG, "empty batch");
     if (!act) return fail(c, LAYA_ERR_ARG, "act is NULL");
-    CK(cudaSetDevice(c->device));
+    DeviceGuard dg;
+    CK(dg.set(c->device));
     int M, G, maxlen;
     int rc = check_seqs(c, seqs, n, &M, &G, &maxlen);
     if (rc) return rc;
@@ -799,7 +851,8 @@ int laya_gpu_forward_device(laya_ctx* c, const laya_batch* bt, float* logits, fl
         return fail(c, LAYA_ERR_ARG, "max_len %u outside [1, %d]", bt->max_len, LAYA_MAX_LEN);
     if (!bt->ids || !bt->cu_seqlens || !bt->cu_markers || !bt->qtypes || !act || (bt->n_markers && (!bt->markers || !logits)))
         return fail(c, LAYA_ERR_ARG, "NULL input or output pointer");
-    CK(cudaSetDevice(c->device));
+    DeviceGuard dg;
+    CK(dg.set(c->device));
     int rc = ensure_workspace(c, (int)bt->n_tokens, (int)bt->n_seqs, (int)bt->n_markers);
     if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);  // 0 = the legacy default stream
@@ -811,7 +864,8 @@ int laya_gpu_forward_device(laya_ctx* c, const laya_batch* bt, float* logits, fl
 
 int laya_gpu_sync(laya_ctx* c) {
     if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
-    CK(cudaSetDevice(c->device));
+    DeviceGuard dg;
+    CK(dg.set(c->device));
     CK(cudaDeviceSynchronize());
     CK(cudaMemcpy(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost));
     return read_err(c);
@@ -821,7 +875,8 @@ int laya_gpu_forward_trace(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_
                            uint32_t K, float* logits, float* act, float* trace) {
     if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
     if (!trace || !act) return fail(c, LAYA_ERR_ARG, "NULL output");
-    CK(cudaSetDevice(c->device));
+    DeviceGuard dg;
+    CK(dg.set(c->device));
     laya_seq sq{ids, L, markers, K, qtype};
     int M, G, maxlen;
     int rc = check_seqs(c, &sq, 1, &M, &G, &maxlen);
@@ -840,14 +895,89 @@ int laya_gpu_forward_trace(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_
     if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
     rc = read_back(c, 1, G, logits, act);
     if (rc) return rc;
-    // The GPU fuses the final norm with the type embedding; the "final" tag
-    // is recovered on the host as temb - type_emb[qtype].
-    std::vector<float> te(3 * D);
-    CK(cudaMemcpy(te.data(), c->type_emb, te.size() * 4, cudaMemcpyDeviceToHost));
-    float* fin = trace + 23 * LD;
-    const float* tmb = trace + 24 * LD;
-    for (size_t i = 0; i < LD; i++) fin[i] = tmb[i] - te[qtype * D + i % D];
     return read_err(c);
+}
+
+int laya_gpu_format_dump(const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers, uint32_t K,
+                         const float* logits, const double* stats, char* text, uint64_t cap, uint64_t* text_len) {
+    if (text_len) *text_len = 0;
+    if (!stats || (L && !ids) || (K && (!markers || !logits)))
+        return fail(nullptr, LAYA_ERR_ARG, "format_dump: NULL input");
+    // The lines the reference's forward prints with --dumpstats, in its
+    // order and formats (src/main.zig:113-130, 2651-2655, 2679-2683,
+    // 2708-2711, 2749-2753, 2771-2777).
+    static const char* const tags[LAYA_TRACE_TAGS] = {
+        "emb", "l0", "l1", "l2", "l3", "l4", "l5", "l6", "l7", "l8", "l9", "l10", "l11", "l12",
+        "l13", "l14", "l15", "l16", "l17", "l18", "l19", "l20", "l21", "final", "temb", "h0", "h1"};
+    std::string out;
+    char line[256];
+    snprintf(line, sizeof line, "[dump] meta L=%u qtype=%u\n", L, qtype);
+    out += line;
+    for (uint32_t i = 0; i < L; i += 8) {
+        out += "[dump] ids";
+        for (uint32_t j = i; j < L && j < i + 8; j++) {
+            snprintf(line, sizeof line, " %u", ids[j]);
+            out += line;
+        }
+        out += "\n";
+    }
+    for (int t = 0; t < LAYA_TRACE_TAGS; t++) {
+        const double* st = stats + 5 * t;  // x[0..2] are f32 values, printed as the reference prints an f32
+        snprintf(line, sizeof line, "[dump] %-5s %.5f %.5f %.5f %.3f %.3f\n", tags[t], (double)(float)st[0],
+                 (double)(float)st[1], (double)(float)st[2], st[3], st[4]);
+        out += line;
+    }
+    out += "[dump] mark";
+    for (uint32_t r = 0; r < K; r++) {
+        snprintf(line, sizeof line, " %u", markers[r]);
+        out += line;
+    }
+    out += "\n[dump] logit";
+    for (uint32_t r = 0; r < K; r++) {
+        snprintf(line, sizeof line, " %.5f", (double)logits[r]);
+        out += line;
+    }
+    out += "\n";
+    if (text_len) *text_len = out.size() + 1;
+    if (!text || cap < out.size() + 1)
+        return fail(nullptr, LAYA_ERR_ARG, "dumpstats: the text needs %zu bytes, %llu given", out.size() + 1,
+                    (unsigned long long)cap);
+    memcpy(text, out.c_str(), out.size() + 1);
+    return LAYA_OK;
+}
+
+int laya_gpu_forward_dumpstats(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers,
+                               uint32_t K, float* logits, float* act, char* text, uint64_t cap, uint64_t* text_len) {
+    if (text_len) *text_len = 0;
+    if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
+    if (!act) return fail(c, LAYA_ERR_ARG, "act is NULL");
+    DeviceGuard dg;
+    CK(dg.set(c->device));
+    laya_seq sq{ids, L, markers, K, qtype};
+    int M, G, maxlen;
+    int rc = check_seqs(c, &sq, 1, &M, &G, &maxlen);
+    if (rc) return rc;
+    if (G && !logits) return fail(c, LAYA_ERR_ARG, "logits is NULL");
+    Batch b;
+    rc = stage_batch(c, &sq, 1, M, G, maxlen, &b);
+    if (rc) return rc;
+    const Outs o = staged_outs(c, 1, nullptr, nullptr);
+    ActMaps am;
+    rc = build_maps(c, M, &am);
+    if (rc) return rc;
+    StatsHook hook{c, (size_t)M * D};
+    cudaError_t e = run_forward(c, b, o, am, c->stream, hook);
+    if (e == cudaSuccess) e = hook.err;
+    if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "forward: %s", cudaGetErrorString(e));
+    double st[LAYA_TRACE_TAGS][5];
+    CK(cudaMemcpyAsync(st, c->d_stats, sizeof st, cudaMemcpyDeviceToHost, c->stream));
+    rc = read_back(c, 1, G, logits, act);
+    if (rc) return rc;
+    rc = read_err(c);
+    if (rc) return rc;
+    return laya_gpu_format_dump(ids, L, qtype, markers, K, logits, &st[0][0], text, cap, text_len) == LAYA_OK
+               ? LAYA_OK
+               : fail(c, LAYA_ERR_ARG, "%s", laya_gpu_last_error(nullptr));
 }
 
 int laya_gpu_forward_dump(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t qtype, const uint32_t* markers,
@@ -855,7 +985,8 @@ int laya_gpu_forward_dump(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t
                           uint16_t* xn_mlp, uint16_t* glu) {
     if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
     if (layer < 0 || layer >= NL) return fail(c, LAYA_ERR_ARG, "layer %d outside [0, %d)", layer, NL);
-    CK(cudaSetDevice(c->device));
+    DeviceGuard dg;
+    CK(dg.set(c->device));
     laya_seq sq{ids, L, markers, K, qtype};
     int M, G, maxlen;
     int rc = check_seqs(c, &sq, 1, &M, &G, &maxlen);
@@ -875,20 +1006,20 @@ int laya_gpu_forward_dump(laya_ctx* c, const uint32_t* ids, uint32_t L, uint32_t
     return read_err(c);
 }
 
-int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, float* act, int iters, void* stream,
-                             float* stage_ms, int* stage_launches) {
+int laya_gpu_forward_profile_launches(laya_ctx* c, const laya_batch* bt, float* logits, float* act, int iters,
+                                      void* stream, float* launch_ms, int* launch_stage, int cap, int* n_launches) {
     if (!c) return fail(nullptr, LAYA_ERR_ARG, "ctx is NULL");
     if (!bt || bt->n_seqs == 0 || bt->n_tokens == 0 || bt->max_len == 0 || bt->max_len > LAYA_MAX_LEN || iters <= 0 ||
-        !stage_ms || !act || (bt->n_markers && !logits))
+        !act || (bt->n_markers && !logits) || cap < 0 || (cap > 0 && (!launch_ms || !launch_stage)))
         return fail(c, LAYA_ERR_ARG, "profile: bad batch or NULL output");
-    CK(cudaSetDevice(c->device));
+    DeviceGuard dg;
+    CK(dg.set(c->device));
     int rc = ensure_workspace(c, (int)bt->n_tokens, (int)bt->n_seqs, (int)bt->n_markers);
     if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);  // 0 = the legacy default stream
     Batch b{bt->ids, bt->cu_seqlens, bt->markers, bt->cu_markers, bt->qtypes, (int)bt->n_seqs, (int)bt->n_tokens,
             (int)bt->n_markers, (int)bt->max_len};
     Outs o{logits, act, nullptr, nullptr};
-    for (int i = 0; i < LAYA_N_STAGES; i++) stage_ms[i] = 0.f;
     ActMaps am;
     rc = build_maps(c, (int)bt->n_tokens, &am);
     if (rc) return rc;
@@ -905,17 +1036,41 @@ int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, f
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile instantiate: %s", cudaGetErrorString(e));
+    const int pairs = (int)(hook.used / 2);
+    std::vector<float> acc(pairs, 0.f);
     for (int it = 0; it < iters && e == cudaSuccess; it++) {
         e = cudaGraphLaunch(exec, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-        if (e == cudaSuccess) hook.collect(stage_ms);
+        if (e == cudaSuccess) hook.collect_each(acc);
     }
     cudaGraphExecDestroy(exec);
     if (e != cudaSuccess) return fail(c, LAYA_ERR_CUDA, "profile run: %s", cudaGetErrorString(e));
-    if (stage_launches)
-        for (int i = 0; i < LAYA_N_STAGES; i++) stage_launches[i] = hook.launches[i];
+    if (n_launches) *n_launches = pairs;
+    for (int i = 0; i < pairs && i < cap; i++) {
+        launch_ms[i] = acc[i];
+        launch_stage[i] = hook.stage[i];
+    }
     CK(cudaMemcpy(c->h_err, c->d_err, 4, cudaMemcpyDeviceToHost));
     return read_err(c);
+}
+
+int laya_gpu_forward_profile(laya_ctx* c, const laya_batch* bt, float* logits, float* act, int iters, void* stream,
+                             float* stage_ms, int* stage_launches) {
+    if (!stage_ms) return fail(c, LAYA_ERR_ARG, "profile: stage_ms is NULL");
+    std::vector<float> ms(512);
+    std::vector<int> st(512);
+    int n = 0;
+    const int rc = laya_gpu_forward_profile_launches(c, bt, logits, act, iters, stream, ms.data(), st.data(), 512, &n);
+    if (rc) return rc;
+    for (int i = 0; i < LAYA_N_STAGES; i++) {
+        stage_ms[i] = 0.f;
+        if (stage_launches) stage_launches[i] = 0;
+    }
+    for (int i = 0; i < n && i < 512; i++) {
+        stage_ms[st[i]] += ms[i];
+        if (stage_launches) stage_launches[st[i]] += st[i] == LAYA_STAGE_TAIL && bt->n_markers ? 3 : 1;
+    }
+    return LAYA_OK;
 }
 
 int laya_gpu_linear(const void* x, const void* w, const float* bias, float* out, int M, int N, int K, int elem_dtype,

@@ -145,7 +145,11 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* __rest
         const int s = find_seq(cu, n_seqs, t);
         seq_of[t] = s;
         p = t - cu[s];
-        if (p >= MAX_POS) {  // sequence lengths are checked on the host; never read past the table
+        // A device-resident offset table is not checked on the host: a token
+        // outside its sequence's run [cu[s], cu[s+1]) (offsets out of order,
+        // cu[0] != 0 or cu[n_seqs] != M) is flagged; its position is taken as
+        // 0 so the RoPE table is never read out of range.
+        if (p < 0 || p >= MAX_POS || t >= cu[s + 1]) {
             atomicOr(err, ERR_BAD_INDEX);
             p = 0;
         }
@@ -205,7 +209,7 @@ template <typename T>
 __global__ void final_kernel(float* __restrict__ x, T* __restrict__ xn, const float* __restrict__ wf,
                              const float* __restrict__ type_emb, const uint32_t* __restrict__ qtypes,
                              const int* __restrict__ seq_of, const float* __restrict__ w1,
-                             const float* __restrict__ b1, int M) {
+                             const float* __restrict__ b1, int M, float* __restrict__ pre_temb, int* err) {
     griddep_wait();
     griddep_launch();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -214,9 +218,14 @@ __global__ void final_kernel(float* __restrict__ x, T* __restrict__ xn, const fl
     Row r;
     load_f32_row(r, x + (size_t)t * D, lane);
     layer_norm(r, wf, nullptr, lane);
-    const uint32_t qt = qtypes[seq_of[t]];
+    if (pre_temb) store_f32_row(pre_temb + (size_t)t * D, r, lane);  // the "final" --dumpstats point
+    uint32_t qt = qtypes[seq_of[t]];
+    if (qt >= 3) {  // device-resident qtypes are not checked on the host
+        if (lane == 0) atomicOr(err, ERR_BAD_INDEX);
+        qt = 0;
+    }
     Row te;
-    load_f32_row(te, type_emb + (size_t)(qt < 3 ? qt : 0) * D, lane);
+    load_f32_row(te, type_emb + (size_t)qt * D, lane);
 #pragma unroll
     for (int i = 0; i < 24; i++) r.v[i] += te.v[i];
     store_f32_row(x + (size_t)t * D, r, lane);
@@ -226,7 +235,47 @@ __global__ void final_kernel(float* __restrict__ x, T* __restrict__ xn, const fl
 
 constexpr int ROWS_PER_BLOCK = 8;  // 256 threads
 
+// dumpStats (src/main.zig:113-121): x[0], x[1], x[2], and the sum and the
+// absolute sum of all n values in f64. One 1024-thread block: coalesced
+// strided partial sums per thread, then a fixed-order tree, so the result
+// does not depend on scheduling.
+constexpr int STATS_THREADS = 1024;
+__global__ void __launch_bounds__(STATS_THREADS) dump_stats_kernel(const float* __restrict__ x, size_t n,
+                                                                   double* __restrict__ out) {
+    __shared__ double ss[STATS_THREADS], sa[STATS_THREADS];
+    griddep_wait();
+    griddep_launch();
+    double sum = 0.0, asum = 0.0;
+    for (size_t i = threadIdx.x; i < n; i += STATS_THREADS) {
+        const double v = x[i];
+        sum += v;
+        asum += fabs(v);
+    }
+    ss[threadIdx.x] = sum;
+    sa[threadIdx.x] = asum;
+    __syncthreads();
+#pragma unroll 1
+    for (int w = STATS_THREADS / 2; w > 0; w >>= 1) {
+        if ((int)threadIdx.x < w) {
+            ss[threadIdx.x] += ss[threadIdx.x + w];
+            sa[threadIdx.x] += sa[threadIdx.x + w];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        out[0] = n > 0 ? x[0] : 0.0;
+        out[1] = n > 1 ? x[1] : 0.0;
+        out[2] = n > 2 ? x[2] : 0.0;
+        out[3] = ss[0];
+        out[4] = sa[0];
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_dump_stats(const float* x, size_t n, double* out5, cudaStream_t s) {
+    return launch_k(dump_stats_kernel, 1, STATS_THREADS, 0, s, x, n, out5);
+}
 
 cudaError_t launch_embed(bool bf16, const uint32_t* ids, const int* cu, int n_seqs, int M, const void* emb,
                          const float* w, float* x, void* xn, const float2* rope, float4* rope_tok, int rope_ld,
@@ -268,15 +317,15 @@ cudaError_t launch_ln(bool bf16, const float* x, void* xn, const float* w, const
 
 cudaError_t launch_final(bool bf16, float* x, void* xn, const float* wf, const float* type_emb,
                          const uint32_t* qtypes, const int* seq_of, const float* w1, const float* b1, int M,
-                         cudaStream_t s) {
+                         float* pre_temb, int* err, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
     const int grid = (M + ROWS_PER_BLOCK - 1) / ROWS_PER_BLOCK;
     if (bf16)
         return launch_k(final_kernel<__nv_bfloat16>, grid, 32 * ROWS_PER_BLOCK, 0, s, x,
-                        static_cast<__nv_bfloat16*>(xn), wf, type_emb, qtypes, seq_of, w1, b1, M);
+                        static_cast<__nv_bfloat16*>(xn), wf, type_emb, qtypes, seq_of, w1, b1, M, pre_temb, err);
     else
         return launch_k(final_kernel<__half>, grid, 32 * ROWS_PER_BLOCK, 0, s, x, static_cast<__half*>(xn), wf,
-                        type_emb, qtypes, seq_of, w1, b1, M);
+                        type_emb, qtypes, seq_of, w1, b1, M, pre_temb, err);
     return cudaGetLastError();
 }
 

@@ -37,21 +37,28 @@ __device__ __forceinline__ int find_seq(const int* cu, int n, int t) {
 // one warp per marker
 __global__ void marker_ln_kernel(const float* __restrict__ x, const int* __restrict__ cu_seqlens,
                                  const uint32_t* __restrict__ markers, const int* __restrict__ cu_markers, int n_seqs,
-                                 int G, const float* __restrict__ w, const float* __restrict__ b,
+                                 int G, int M, const float* __restrict__ w, const float* __restrict__ b,
                                  float* __restrict__ mv, int* err) {
     griddep_wait();
     griddep_launch();
     const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (g >= G) return;
+    // Device-resident offsets are not checked on the host. The marker must
+    // lie in its sequence's marker run and inside the sequence, and the
+    // sequence inside the M rows of x; otherwise the marker is flagged and
+    // its vector zeroed, and no row outside x is read.
     const int s = find_seq(cu_markers, n_seqs, g);
-    const int L = cu_seqlens[s + 1] - cu_seqlens[s];
-    uint32_t m = markers[g];
-    if (m >= (uint32_t)L) {
+    const int rows = M >= 0 ? M : cu_seqlens[n_seqs];
+    const int cs = cu_seqlens[s], L = cu_seqlens[s + 1] - cs;
+    const uint32_t m = markers[g];
+    if (g < cu_markers[s] || g >= cu_markers[s + 1] || cs < 0 || L <= 0 || cs > rows - L || m >= (uint32_t)L) {
         if (lane == 0) atomicOr(err, ERR_BAD_INDEX);
-        m = 0;
+#pragma unroll
+        for (int i = 0; i < 24; i++) mv[(size_t)g * D + i * 32 + lane] = 0.f;
+        return;
     }
-    const float* row = x + (size_t)(cu_seqlens[s] + m) * D;
+    const float* row = x + (size_t)(cs + m) * D;
     float v[24];
 #pragma unroll
     for (int i = 0; i < 24; i++) v[i] = row[i * 32 + lane];
@@ -173,18 +180,29 @@ __global__ void __cluster_dims__(1, 1, SC_SPLIT) __launch_bounds__(256)
 constexpr int ACT_THREADS = 1024, ACT_SLICES = ACT_THREADS / 256, ACT_IN = D + 4;
 __global__ void __launch_bounds__(ACT_THREADS) act_kernel(const float* __restrict__ x,
                                                           const int* __restrict__ cu_seqlens,
-                                                          const int* __restrict__ cu_markers,
+                                                          const int* __restrict__ cu_markers, int G, int M,
                                                           const float* __restrict__ partial, TailWeights w,
                                                           float* __restrict__ logits, float* __restrict__ act,
-                                                          float* __restrict__ pooled) {
+                                                          float* __restrict__ pooled, int* err) {
     __shared__ float lg[MAX_MARKERS_PER_SEQ];
     __shared__ float act_in[ACT_IN];
     __shared__ float hpart[ACT_SLICES][256];
     __shared__ float a2[2];
     griddep_wait();
     griddep_launch();
-    const int s = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int gb = cu_markers[s], K = min(cu_markers[s + 1] - gb, MAX_MARKERS_PER_SEQ);
+    const int s = blockIdx.x, n_seqs = gridDim.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // Device-resident offsets are not checked on the host. A marker run that
+    // is not inside [0, G) or is longer than MAX_MARKERS_PER_SEQ is flagged
+    // and scored as empty (its logits are not written); a [CLS] row outside
+    // the M rows of x is flagged and read as zeros.
+    const int gb = cu_markers[s], ge = cu_markers[s + 1];
+    const int rows = M >= 0 ? M : cu_seqlens[n_seqs];
+    const int cs = cu_seqlens[s];
+    const bool bad_k = gb < 0 || ge < gb || ge > G || ge - gb > MAX_MARKERS_PER_SEQ;
+    const bool bad_cls = cs < 0 || cs >= rows;
+    const bool bad_tab = s == 0 && (cu_markers[0] != 0 || cu_markers[n_seqs] != G || cu_seqlens[0] != 0);
+    if (tid == 0 && (bad_k || bad_cls || bad_tab)) atomicOr(err, ERR_BAD_INDEX);
+    const int K = bad_k ? 0 : ge - gb;
     for (int r = tid; r < K; r += ACT_THREADS) {
         float v = 0.f;
         for (int c = 0; c < SCORER_GROUPS; c++) v += partial[(size_t)(gb + r) * SCORER_GROUPS + c];
@@ -192,10 +210,11 @@ __global__ void __launch_bounds__(ACT_THREADS) act_kernel(const float* __restric
         lg[r] = v;
         logits[gb + r] = v;
     }
-    const float* cls = x + (size_t)cu_seqlens[s] * D;
+    const float* cls = x + (size_t)(bad_cls ? 0 : cs) * D;
     for (int c = tid; c < D; c += ACT_THREADS) {
-        act_in[c] = cls[c];
-        pooled[(size_t)s * D + c] = cls[c];
+        const float v = bad_cls ? 0.f : cls[c];
+        act_in[c] = v;
+        pooled[(size_t)s * D + c] = v;
     }
     __syncthreads();
     if (tid == 0) {
@@ -271,19 +290,19 @@ __global__ void __launch_bounds__(ACT_THREADS) act_kernel(const float* __restric
 }  // namespace
 
 cudaError_t launch_tail(const float* x, const int* cu_seqlens, const uint32_t* markers, const int* cu_markers,
-                        int n_seqs, int G, const TailWeights& w, float* mv, float* partial, float* logits, float* act,
-                        float* pooled, int* err, cudaStream_t s) {
+                        int n_seqs, int G, int M, const TailWeights& w, float* mv, float* partial, float* logits,
+                        float* act, float* pooled, int* err, cudaStream_t s) {
     if (n_seqs <= 0) return cudaSuccess;
     if (G > 0) {
         cudaError_t e = launch_k(marker_ln_kernel, (G + 7) / 8, 256, 0, s, x, cu_seqlens, markers, cu_markers, n_seqs,
-                                 G, w.s0w, w.s0b, mv, err);
+                                 G, M, w.s0w, w.s0b, mv, err);
         if (e != cudaSuccess) return e;
         e = launch_k(scorer_kernel, dim3((G + SC_M - 1) / SC_M, D / SC_N, SC_SPLIT), 256, 0, s, mv, G, w.s1w, w.s1b,
                      w.s3w, partial);
         if (e != cudaSuccess) return e;
     }
-    return launch_k(act_kernel, n_seqs, ACT_THREADS, 0, s, x, cu_seqlens, cu_markers, partial, w, logits, act,
-                    pooled);
+    return launch_k(act_kernel, n_seqs, ACT_THREADS, 0, s, x, cu_seqlens, cu_markers, G, M, partial, w, logits, act,
+                    pooled, err);
 }
 
 }  // namespace laya

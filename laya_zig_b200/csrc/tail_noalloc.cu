@@ -18,6 +18,7 @@
 // every element a call reads is first written by the same call, so nothing
 // needs clearing, but calls that overlap on the GPU (on different streams,
 // or from different threads) race on it.
+#include <atomic>
 #include <cstdio>
 
 #include "../../include/laya_gpu.h"
@@ -32,8 +33,10 @@ static __device__ __align__(256) float g_tail_scratch[SCRATCH_FLOATS];
 
 // Device address of g_tail_scratch per device, resolved on the first call on
 // that device with that device current (in host code the symbol is only a
-// stand-in, not an address a kernel could use).
-static float* g_scratch_ptr[64] = {nullptr};
+// stand-in, not an address a kernel could use). Atomic, because two host
+// threads may make their first calls on one device at the same time; both
+// then resolve and store the same address.
+static std::atomic<float*> g_scratch_ptr[64];
 
 // Context pieces the tail needs (defined with the context in laya_gpu.cu).
 int laya_ctx_tail_view(laya_ctx* c, TailWeights* w, int* device, int** d_err);
@@ -43,11 +46,12 @@ extern "C" LAYA_API int laya_gpu_decision_tail_noalloc(laya_ctx* ctx, const floa
                                                        const uint32_t* markers, const int32_t* cu_markers,
                                                        uint32_t n_seqs, uint32_t n_markers, float* logits,
                                                        float* act, float* pooled, void* stream) {
+    if (!ctx) return laya_ctx_fail(nullptr, LAYA_ERR_ARG, "decision tail: ctx is NULL");
     TailWeights w;
     int device = 0;
     int* d_err = nullptr;
-    if (!ctx || laya_ctx_tail_view(ctx, &w, &device, &d_err) != LAYA_OK)
-        return laya_ctx_fail(ctx, LAYA_ERR_ARG, "decision tail: ctx is NULL");
+    if (laya_ctx_tail_view(ctx, &w, &device, &d_err) != LAYA_OK)
+        return laya_ctx_fail(ctx, LAYA_ERR_ARG, "decision tail: the context has no tail weights");
     if (!hidden || !cu_seqlens || !cu_markers || !act || !pooled || (n_markers && (!markers || !logits)))
         return laya_ctx_fail(ctx, LAYA_ERR_ARG, "decision tail: NULL input or output pointer");
     if (n_seqs == 0) return laya_ctx_fail(ctx, LAYA_ERR_ARG, "decision tail: no sequences");
@@ -58,18 +62,29 @@ extern "C" LAYA_API int laya_gpu_decision_tail_noalloc(laya_ctx* ctx, const floa
         return laya_ctx_fail(ctx, LAYA_ERR_ARG, msg);
     }
     if (device < 0 || device >= 64) return laya_ctx_fail(ctx, LAYA_ERR_NO_DEVICE, "decision tail: device index");
+    // The context's device is made current for the call and the caller's
+    // current device given back before returning.
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    struct Restore {
+        int dev;
+        ~Restore() {
+            if (dev >= 0) cudaSetDevice(dev);
+        }
+    } restore{prev};
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return laya_ctx_fail(ctx, LAYA_ERR_CUDA, cudaGetErrorString(e));
-    if (!g_scratch_ptr[device]) {
+    float* mv = g_scratch_ptr[device].load(std::memory_order_relaxed);
+    if (!mv) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_tail_scratch);
         if (e != cudaSuccess || !p) return laya_ctx_fail(ctx, LAYA_ERR_CUDA, "cudaGetSymbolAddress(g_tail_scratch) failed");
-        g_scratch_ptr[device] = static_cast<float*>(p);
+        mv = static_cast<float*>(p);
+        g_scratch_ptr[device].store(mv, std::memory_order_relaxed);
     }
-    float* mv = g_scratch_ptr[device];
     float* partial = mv + MV_FLOATS;
     e = launch_tail(hidden, cu_seqlens, markers, reinterpret_cast<const int*>(cu_markers), (int)n_seqs,
-                    (int)n_markers, w, mv, partial, logits, act, pooled, d_err, static_cast<cudaStream_t>(stream));
+                    (int)n_markers, -1, w, mv, partial, logits, act, pooled, d_err, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return laya_ctx_fail(ctx, LAYA_ERR_CUDA, cudaGetErrorString(e));
     return LAYA_OK;
 }

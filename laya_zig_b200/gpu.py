@@ -100,8 +100,16 @@ def _load():
     L.laya_gpu_linear.restype = I
     L.laya_gpu_forward_profile.argtypes = [P, ctypes.POINTER(_Batch), P, P, I, P, P, P]
     L.laya_gpu_forward_profile.restype = I
+    L.laya_gpu_forward_profile_launches.argtypes = [P, ctypes.POINTER(_Batch), P, P, I, P, P, P, I, P]
+    L.laya_gpu_forward_profile_launches.restype = I
     L.laya_gpu_forward_dump.argtypes = [P, P, U, U, P, U, I, P, P, P, P, P, P]
     L.laya_gpu_forward_dump.restype = I
+    L.laya_gpu_forward_dumpstats.argtypes = [P, P, U, U, P, U, P, P, ctypes.c_char_p, ctypes.c_uint64,
+                                             ctypes.POINTER(ctypes.c_uint64)]
+    L.laya_gpu_forward_dumpstats.restype = I
+    L.laya_gpu_format_dump.argtypes = [P, U, U, P, U, P, P, ctypes.c_char_p, ctypes.c_uint64,
+                                       ctypes.POINTER(ctypes.c_uint64)]
+    L.laya_gpu_format_dump.restype = I
     L.laya_gpu_decision_tail_noalloc.argtypes = [P, P, P, P, P, U, U, P, P, P, P]
     L.laya_gpu_decision_tail_noalloc.restype = I
     return L
@@ -256,6 +264,20 @@ class LayaGPU:
                                                _p(act), _p(trace)))
         return logits[:K], act, trace
 
+    def forward_dumpstats(self, ids, qtype: int, markers):
+        """(logits, act, text): forward() plus the `[dump]` lines the
+        reference prints with --dumpstats (src/main.zig:113-130, 2651-2777),
+        fingerprints computed on the device."""
+        ids, markers = _u32(ids), _u32(markers)
+        K, L = len(markers), len(ids)
+        logits, act = np.zeros(max(K, 1), np.float32), np.zeros(2, np.float32)
+        cap = 256 + 80 * (L // 8 + 1) + 96 * 27 + 24 * K
+        need = ctypes.c_uint64(0)
+        buf = ctypes.create_string_buffer(cap)
+        self._check(lib.laya_gpu_forward_dumpstats(self._h, _p(ids), L, int(qtype), _p(markers), K, _p(logits),
+                                                   _p(act), buf, cap, ctypes.byref(need)))
+        return logits[:K], act, buf.value.decode()
+
     def forward_dump(self, ids, qtype: int, markers, layer: int):
         """Every intermediate of encoder layer `layer` as f32 arrays: xn_attn,
         qkv, ctx, x_mid, xn_mlp, glu (see laya_gpu_forward_dump)."""
@@ -307,6 +329,20 @@ class LayaGPU:
         return dict(zip(STAGES, ms.tolist())), dict(zip(STAGES, n.tolist()))
 
 
+    def profile_launches(self, batch: "DeviceBatch", logits_ptr: int, act_ptr: int, iters: int = 1,
+                         stream: int = 0):
+        """[(stage, summed ms over `iters`)] for every launch of one forward,
+        in launch order (the same event-pair capture as `profile`)."""
+        cap = 512
+        ms = np.zeros(cap, np.float32)
+        st = np.zeros(cap, np.int32)
+        n = ctypes.c_int(0)
+        self._check(lib.laya_gpu_forward_profile_launches(self._h, ctypes.byref(batch.c), logits_ptr or None,
+                                                          act_ptr or None, int(iters), stream or None, _p(ms), _p(st),
+                                                          cap, ctypes.byref(n)))
+        return [(STAGES[int(st[i])], float(ms[i])) for i in range(min(n.value, cap))]
+
+
 class DeviceBatch:
     """Shape + device pointers of a packed batch for LayaGPU.forward_device."""
 
@@ -328,6 +364,22 @@ def pack(decisions) -> Dict[str, np.ndarray]:
         "qtypes": np.array([d.qtype for d in decisions], dtype=np.uint32),
         "max_len": int(lens.max()),
     }
+
+
+def format_dump(ids, qtype: int, markers, logits, stats) -> str:
+    """The reference's `[dump]` text (src/main.zig:113-130) for given
+    fingerprints stats[27][5] (x0, x1, x2, sum, abs-sum per tag), host only."""
+    ids, markers = _u32(ids), _u32(markers)
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    st = np.ascontiguousarray(stats, dtype=np.float64)
+    assert st.shape == (len(TRACE_TAGS), 5)
+    cap = 256 + 80 * (len(ids) // 8 + 1) + 96 * 27 + 24 * len(markers)
+    buf = ctypes.create_string_buffer(cap)
+    rc = lib.laya_gpu_format_dump(_p(ids), len(ids), int(qtype), _p(markers), len(markers), _p(logits), _p(st), buf,
+                                  cap, None)
+    if rc != LAYA_OK:
+        raise _error(rc, lib.laya_gpu_last_error(None).decode())
+    return buf.value.decode()
 
 
 def linear(x_ptr: int, w_ptr: int, bias_ptr: int, out_ptr: int, M: int, N: int, K: int, dtype: str = "BF16",

@@ -30,6 +30,14 @@ Token ids are drawn with numpy's PCG64 from the workload's seed. Each
 sequence starts with [CLS] (id 2), ends with [SEP] (id 1) and carries [MASK]
 (id 4) at its option markers, the shape `buildSequence`
 (src/main.zig:2842-2911) gives real prompts.
+
+With random weights the hidden states of identical [MASK] tokens differ
+only through their weakly mixed context, so the option logits of such a
+decision lie within about 1e-2 of each other and their order is a near-tie
+that 16-bit tensor-core operands cannot reproduce. `option_tokens=True`
+puts a random token at each marker instead, as the distinct option text
+after each <mask> does for a trained model: the logits then spread about
+15x wider (median top-two margin 6e-2 against 5e-3 on the 64 x 180 batch).
 """
 from __future__ import annotations
 
@@ -193,39 +201,47 @@ class Decision:
     qtype: int            # 0 choice, 1 score, 2 noul
 
 
-def _decision(rng: np.random.Generator, L: int, markers: Sequence[int], qtype: int) -> Decision:
+def _decision(rng: np.random.Generator, L: int, markers: Sequence[int], qtype: int,
+              option_tokens: bool = False) -> Decision:
+    """Token ids uniform in [0, VOCAB) with [CLS] first and [SEP] last; the
+    marker positions hold [MASK], or, with option_tokens, ids drawn at random
+    (one per marker, after the sequence's ids)."""
     ids = rng.integers(0, VOCAB, size=L, dtype=np.int64).astype(np.uint32)
     ids[0] = CLS_ID
     if L > 1:
         ids[L - 1] = SEP_ID
     mk = np.asarray(markers, dtype=np.uint32)
-    ids[mk] = MASK_ID
+    if option_tokens:
+        ids[mk] = rng.integers(5, VOCAB, size=len(mk), dtype=np.int64).astype(np.uint32)
+    else:
+        ids[mk] = MASK_ID
     return Decision(ids=ids, markers=mk, qtype=int(qtype))
 
 
-def parity_decision(seed: int = 1) -> Decision:
+def parity_decision(seed: int = 1, option_tokens: bool = False) -> Decision:
     """Batch 1 x seq 64, four markers at fixed offsets, qtype 0."""
     rng = np.random.Generator(np.random.PCG64(seed))
-    return _decision(rng, 64, [8, 16, 24, 32], 0)
+    return _decision(rng, 64, [8, 16, 24, 32], 0, option_tokens)
 
 
 SNAKE_MARKERS = [20 + 18 * r for r in range(8)]
 
 
-def snake_batch(batch: int = 64, seed: int = 2, lo: int = 175, hi: int = 180) -> List[Decision]:
+def snake_batch(batch: int = 64, seed: int = 2, lo: int = 175, hi: int = 180,
+                option_tokens: bool = False) -> List[Decision]:
     """Snake-style decisions: lengths uniform in [lo, hi], 8 option markers
     at fixed offsets inside the head segment, qtype cycling 0/1/2."""
     rng = np.random.Generator(np.random.PCG64(seed))
     lens = rng.integers(lo, hi + 1, size=batch)
     mk = [m for m in SNAKE_MARKERS if m < lo - 1]
-    return [_decision(rng, int(L), mk, b % 3) for b, L in enumerate(lens)]
+    return [_decision(rng, int(L), mk, b % 3, option_tokens) for b, L in enumerate(lens)]
 
 
-def long_decision(L: int = 8192, K: int = 16, seed: int = 3) -> Decision:
+def long_decision(L: int = 8192, K: int = 16, seed: int = 3, option_tokens: bool = False) -> Decision:
     """One long sequence with K markers at random distinct positions."""
     rng = np.random.Generator(np.random.PCG64(seed))
     mk = np.sort(rng.choice(np.arange(1, L - 1), size=K, replace=False))
-    return _decision(rng, L, mk.tolist(), 0)
+    return _decision(rng, L, mk.tolist(), 0, option_tokens)
 
 
 def sweep_decisions(n: int = 65536, seed: int = 4, lo: int = 128, hi: int = 512) -> List[Decision]:

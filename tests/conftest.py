@@ -45,13 +45,23 @@ def gpu_model(weights):
     m.close()
 
 
+@pytest.fixture(scope="session")
+def c3_oracle(oracle_model):
+    """The oracle's outputs (with final hidden states) for the 64-decision
+    Snake-style batch, computed once per session."""
+    from laya_zig_b200 import synth
+    return [oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True) for d in synth.snake_batch(64)]
+
+
 def golden_cases():
     import json
     out = {}
     for f in sorted(os.listdir(GOLDEN)):
         if f.endswith(".json"):
             with open(os.path.join(GOLDEN, f)) as fh:
-                out[f[:-5]] = json.load(fh)
+                g = json.load(fh)
+            if "case" in g:  # refcheck forward fixtures (make_golden.py), not separated.json
+                out[f[:-5]] = g
     return out
 
 

@@ -21,8 +21,8 @@ the untempered option probabilities, the act pair, and the final hidden rows
 at [CLS], the markers and the last token; the complete final hidden state of
 the parity case is stored as float32 .npy.
 
-Usage (needs the reference checkout; takes several minutes of CPython):
-    python tests/golden/make_golden.py --reference /root/reference
+Usage (needs a laya-zig checkout; takes several minutes of CPython):
+    python tests/golden/make_golden.py --reference <path to the laya-zig checkout>
 """
 from __future__ import annotations
 
@@ -145,7 +145,7 @@ def run_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path to a laya-zig checkout (holds tools/refcheck.py)")
     ap.add_argument("--out", default=HERE)
     ap.add_argument("--cases", default=",".join(cases().keys()))
     args = ap.parse_args()

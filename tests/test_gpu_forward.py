@@ -92,14 +92,13 @@ def test_gpu_matches_refcheck_golden(name, gpu_model):
     assert np.abs(out.act - np.array(g["act"])).max() <= PROB_TOL
 
 
-def test_snake_batch_parity(gpu_model, oracle_model):
+def test_snake_batch_parity(gpu_model, c3_oracle):
     """Batch 64 x 175-180 tokens, 8 markers each, one packed pass vs the oracle per sequence."""
     from laya_zig_b200 import synth
     batch = synth.snake_batch(64)
     outs = gpu_model.forward_batch(batch, want_pooled=True, want_hidden=True)
     worst = {}
-    for i, (d, g) in enumerate(zip(batch, outs)):
-        r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+    for i, (d, g, r) in enumerate(zip(batch, outs, c3_oracle)):
         e = _compare(g, r, "seq %d" % i)
         for k, v in e.items():
             worst[k] = max(worst.get(k, 0.0), v)

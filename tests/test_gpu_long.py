@@ -17,13 +17,23 @@ pytestmark = pytest.mark.gpu
 
 
 def test_long_context_8192(gpu_model, oracle_model):
+    """Random tokens at the 16 markers (the decision of tests/golden/
+    separated.json), so its option logits are well separated and the
+    argmax is asserted without a margin clause."""
+    import json
+    import os
+    from conftest import GOLDEN
     from laya_zig_b200 import synth
     from test_gpu_forward import _compare
-    d = synth.long_decision(8192, 16, seed=3)
+    seed = json.load(open(os.path.join(GOLDEN, "separated.json")))["c4"]["seed"]
+    d = synth.long_decision(8192, 16, seed=seed, option_tokens=True)
     g = gpu_model.forward(d.ids, d.qtype, d.markers, want_hidden=True)
     r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+    assert int(np.argmax(g.logits)) == int(np.argmax(r["logits"]))
     err = _compare(g, r, "L=8192")
-    print("long-context errors", err)
+    s = np.sort(r["logits"].astype(np.float64))
+    print("long-context errors", err, "top-two margin %.3e" % (s[-1] - s[-2]))
+    assert s[-1] - s[-2] >= 10 * err["logits"]
 
 
 def test_full_bucket_packing_invariance(gpu_model, oracle_model):

@@ -4,9 +4,11 @@ reference's own golden ids (tests/golden/tokcheck.jsonl, a copy of the
 reference's tools/tokcheck.jsonl).
 
 The vocabulary tests need the model's tokenizer.json (256,000 entries,
-580,604 merges); they look for it at $LAYA_TOKENIZER_JSON or in the
-reference checkout and are skipped where neither exists. The synthetic
-vocabulary tests need nothing."""
+580,604 merges), which this repository does not ship. They read it from
+$LAYA_TOKENIZER_JSON, else from tokenizer/tokenizer.json of a laya-zig
+checkout named by $LAYA_REFERENCE or lying beside this repository as
+../reference, and are skipped where none exists. The synthetic vocabulary
+tests need nothing."""
 import json
 import os
 
@@ -15,7 +17,14 @@ import pytest
 
 from conftest import ROOT
 
-REAL_JSON = os.environ.get("LAYA_TOKENIZER_JSON", "/root/reference/tokenizer/tokenizer.json")
+def _tokenizer_json() -> str:
+    if os.environ.get("LAYA_TOKENIZER_JSON"):
+        return os.environ["LAYA_TOKENIZER_JSON"]
+    ref = os.environ.get("LAYA_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
+    return os.path.join(ref, "tokenizer", "tokenizer.json")
+
+
+REAL_JSON = _tokenizer_json()
 needs_vocab = pytest.mark.skipif(not os.path.exists(REAL_JSON), reason="tokenizer.json not available")
 
 
