@@ -315,6 +315,7 @@ def run_sweep(args, world: int):
         a = ac.cpu().numpy()
         assert np.isfinite(a).all() and np.allclose(a.sum(1), 1, atol=1e-4), "bad act output"
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    ranks = per_rank(world, float(t.item()), clk, float(tokens))
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
@@ -333,11 +334,28 @@ def run_sweep(args, world: int):
                    "global_batch": n, "seq_len": "128-512", "parallelism": "replicas dp%d (no collective)" % world,
                    "rank0_buckets": len(mine), "rank0_tokens": tokens,
                    "l2": "every bucket's activations exceed L2"},
+        "per_rank": [{"rank": r["rank"], "ms": r["ms"], "sm_mhz": r["sm_mhz"], "tokens": int(r["extra"])}
+                     for r in ranks],
         "rank0_tokens_per_s": tokens * args.steps / (t_max / 1e3),
         "rank0_tflops": flops * args.steps / (t_max / 1e3) / 1e12,
         "gpu_launches": len(mine) * 171 * args.steps,
         "clocks": clk,
     }), flush=True)
+
+
+def per_rank(world, t_ms, clk, extra=0.0):
+    """[{rank, ms, sm_mhz, extra}] gathered from every rank (one small NCCL
+    all-gather; the same call on every rank)."""
+    import torch
+    import torch.distributed as dist
+    v = torch.tensor([t_ms, clk.get("sm_mhz") or -1.0, extra], dtype=torch.float64, device="cuda")
+    if world <= 1:
+        rows = [v]
+    else:
+        rows = [torch.zeros_like(v) for _ in range(world)]
+        dist.all_gather(rows, v)
+    return [{"rank": r, "ms": float(x[0]), "sm_mhz": float(x[1]) if x[1] >= 0 else None, "extra": float(x[2])}
+            for r, x in enumerate(rows)]
 
 
 def _clock_region(local):
@@ -594,6 +612,7 @@ def main():
     clk = clocks.stop()
     model.sync()
     t_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    ranks = per_rank(world, t_ms, clk)
     t = torch.tensor([t_ms], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -696,6 +715,7 @@ def main():
         "gpu_launches": (sum(len(v) for v in fam.values()) + (2 if G else 0)) * args.steps,
         "clocks": clk,
         "family_ms_per_step": {k: sum(v) * attr for k, v in fam.items()},
+        "per_rank": [{"rank": r["rank"], "ms_per_step": r["ms"] / args.steps, "sm_mhz": r["sm_mhz"]} for r in ranks],
         "whole_step_tflops": flops_step / (step_ms / 1e3) / 1e12,
         "secondary_rooflines": secondary,
     }

@@ -109,7 +109,7 @@ __device__ __forceinline__ void load_tile(T* tile, const T* src, int ld, int r0,
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
                                                             const int* __restrict__ cu_seqlens, int M, int max_len,
-                                                            int window, int* err) {
+                                                            int window, int* err, int long_len) {
     extern __shared__ __align__(128) uint8_t att_smem[];  // Q tile, then NST K tiles, then NST V tiles
     T* sQ = reinterpret_cast<T*>(att_smem);
     T* sK = sQ + QB * 64;
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
         return;
     }
     const int q0 = blockIdx.x * QB;
-    if (q0 >= L) return;
+    if (q0 >= L || L >= long_len) return;
     griddep_wait();  // qkv comes from the preceding projection
     const int ld = 3 * D;
     const T* base = qkv + (size_t)start * ld;
@@ -307,15 +307,27 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
 }  // namespace
 
 cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* cu_seqlens, int n_seqs, int M,
-                             int max_len, int window, int* err, cudaStream_t stream) {
+                             int max_len, int window, int* err, cudaStream_t stream, int long_len) {
     if (n_seqs <= 0 || max_len <= 0) return cudaSuccess;
     dim3 grid((max_len + QB - 1) / QB, H, n_seqs);
     if (bf16)
         return launch_k(attention_kernel<__nv_bfloat16>, grid, THREADS, SMEM_BYTES, stream,
                         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, M,
-                        max_len, window, err);
+                        max_len, window, err, long_len);
     return launch_k(attention_kernel<__half>, grid, THREADS, SMEM_BYTES, stream, static_cast<const __half*>(qkv),
-                    static_cast<__half*>(out), cu_seqlens, M, max_len, window, err);
+                    static_cast<__half*>(out), cu_seqlens, M, max_len, window, err, long_len);
+}
+
+int attention_tc_min_len() {
+    static const int v = [] {
+        const char* e = getenv("LAYA_ATTN_TC_MIN_LEN");
+        if (e && *e) {
+            const int x = atoi(e);
+            return x <= 0 ? 0x7fffffff : x;
+        }
+        return 1024;
+    }();
+    return v;
 }
 
 cudaError_t attention_prepare() {
@@ -323,6 +335,7 @@ cudaError_t attention_prepare() {
                                          SMEM_BYTES);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(attention_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess) e = attention_tc_prepare();
     return e;
 }
 

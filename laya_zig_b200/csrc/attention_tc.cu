@@ -1,0 +1,384 @@
+// attention_tc.cu -- tensor-core (tcgen05) attention for long sequences.
+//
+// Replaces attWorker (src/main.zig:2431-2489) on global-attention layers for
+// sequences of at least attention_tc_min_len() tokens. Each CTA takes two
+// 128-row query tiles of one head of one sequence and streams the
+// sequence's keys and values through shared memory in tiles of 128:
+//
+//   warp 8      TMA producer: both Q tiles once, then K_j and V_j (128 x 64
+//               16-bit boxes, 128-byte swizzle) into a KV_STAGES-deep ring.
+//   warp 9      TMEM owner and MMA issuer: S_q = Q_q K_j^T (M 128, N 128,
+//               K 64) into TMEM, then O_q = P_q V_j (M 128, N 64, K 128)
+//               with P from shared memory and V read MN-major.
+//   warps 0-7   two softmax warpgroups, one per query tile; thread t of a
+//               group owns query row t (its TMEM lane). Per key tile: the
+//               row maximum (first pass over S), the previous tile's O_q
+//               folded into the register accumulator with its rescale
+//               factor, then p = 2^(s*log2(e)/8 - m*log2(e)/8) with the row
+//               sum in f32 and P rounded to 16 bits into shared memory in the
+//               K-major swizzled layout the MMA reads (second pass).
+//
+// The softmax is the online form of the mma.sync kernel (attention.cu): same
+// scale, same exp2 argument, normalised once at the end as the reference
+// does (2479-2486); only the MMA shapes and so the summation order differ.
+// Keys past the sequence end are masked to -inf; query rows past it are
+// computed and not stored. Every wait is bounded (common.cuh): a CTA that
+// gives up sets the error word, drains its own TMA loads and MMAs, frees
+// TMEM and exits.
+#include <type_traits>
+
+#include "attention.cuh"
+
+namespace laya {
+namespace {
+
+constexpr int TQ = 128;        // query rows per tile (one TMEM lane each)
+constexpr int TK = 128;        // keys per tile
+constexpr int NQT = 2;         // query tiles per CTA
+constexpr int KV_STAGES = 3;
+constexpr int TC_THREADS = 320;
+constexpr int TILE_BYTES = TQ * HD * 2;            // 16 KB: a 128 x 64 16-bit box
+constexpr int P_BYTES = TQ * TK * 2;               // 32 KB: 128 x 128 16-bit, two 64-key swizzle atoms
+constexpr int SMEM_Q = 0;
+constexpr int SMEM_K = SMEM_Q + NQT * TILE_BYTES;
+constexpr int SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
+constexpr int SMEM_P = SMEM_V + KV_STAGES * TILE_BYTES;
+constexpr int SMEM_BAR = SMEM_P + NQT * P_BYTES;
+constexpr int SMEM_TC = SMEM_BAR + 256 + 1024;     // barriers, TMEM slot, 1 KB alignment slack
+constexpr uint32_t TMEM_COLS = 512;                // S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
+constexpr uint32_t IDESC_S_BF16 = idesc_f16(TQ, TK, true);
+constexpr uint32_t IDESC_S_F16 = idesc_f16(TQ, TK, false);
+// P . V: B (= V) is MN-major (head dim contiguous): transpose-B bit 16.
+constexpr uint32_t IDESC_O_BF16 = idesc_f16(TQ, HD, true) | (1u << 16);
+constexpr uint32_t IDESC_O_F16 = idesc_f16(TQ, HD, false) | (1u << 16);
+
+struct Bars {
+    uint64_t q_full;
+    uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
+    uint64_t s_full[NQT], p_full[NQT], o_full[NQT];
+    uint64_t drain;
+    uint32_t tmem;
+    int abort;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack16(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack16<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack16<__half>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Bounded wait for an mbarrier phase with no abort flag (teardown drains).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+            atomicOr(err, ERR_WAIT_TIMEOUT);
+            return;
+        }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap qkv_map, T* __restrict__ out,
+                        const int* __restrict__ cu_seqlens, int M, int max_len, int min_len, int* err) {
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars* bar = reinterpret_cast<Bars*>(smem + SMEM_BAR);
+    volatile int* abort_flag = &bar->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int seq = blockIdx.z, h = blockIdx.y;
+    const int start = cu_seqlens[seq];  // batch offsets: written before the forward starts
+    const int L = cu_seqlens[seq + 1] - start;
+    if (start < 0 || L < 0 || L > max_len || start > M - L) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_BAD_INDEX);
+        return;
+    }
+    const int q0 = blockIdx.x * (NQT * TQ);
+    if (L < min_len || q0 >= L) return;  // shorter sequences are the mma.sync kernel's
+    const int nq = min(NQT, (L - q0 + TQ - 1) / TQ);  // query tiles with rows in the sequence
+    const int nkt = (L + TK - 1) / TK;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar->q_full, 1);
+        for (int s = 0; s < KV_STAGES; s++) {
+            mbar_init(&bar->kv_full[s], 1);
+            mbar_init(&bar->kv_empty[s], 1);
+        }
+        for (int q = 0; q < NQT; q++) {
+            mbar_init(&bar->s_full[q], 1);
+            mbar_init(&bar->p_full[q], TQ);
+            mbar_init(&bar->o_full[q], 1);
+        }
+        mbar_init(&bar->drain, 1);
+        bar->abort = 0;
+        fence_barrier_init();
+        fence_proxy_async();
+    }
+    if (warp == 8 && lane == 0) prefetch_tmap(&qkv_map);
+    if (warp == 9) {
+        tmem_alloc(&bar->tmem, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bar->tmem;
+    griddep_launch();
+    griddep_wait();  // qkv comes from the preceding projection
+
+    if (warp == 8) {
+        // ---------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            int issued_phase[KV_STAGES];
+            for (int s = 0; s < KV_STAGES; s++) issued_phase[s] = -1;
+            mbar_arrive_expect_tx(&bar->q_full, nq * TILE_BYTES);
+            for (int q = 0; q < nq; q++)
+                tma_load_2d(smem + SMEM_Q + q * TILE_BYTES, &qkv_map, &bar->q_full, h * HD, start + q0 + q * TQ);
+            for (int j = 0; j < nkt && !*abort_flag; j++) {
+                const int s = j % KV_STAGES;
+                const uint32_t ph = (j / KV_STAGES) & 1;
+                if (!mbar_wait(&bar->kv_empty[s], ph ^ 1, err, abort_flag)) break;
+                mbar_arrive_expect_tx(&bar->kv_full[s], 2 * TILE_BYTES);
+                tma_load_2d(smem + SMEM_K + s * TILE_BYTES, &qkv_map, &bar->kv_full[s], D + h * HD, start + j * TK);
+                tma_load_2d(smem + SMEM_V + s * TILE_BYTES, &qkv_map, &bar->kv_full[s], 2 * D + h * HD,
+                            start + j * TK);
+                issued_phase[s] = (int)ph;
+            }
+            // every load issued lands before shared memory goes away
+            drain_wait(&bar->q_full, 0, err);
+            for (int s = 0; s < KV_STAGES; s++)
+                if (issued_phase[s] >= 0) drain_wait(&bar->kv_full[s], (uint32_t)issued_phase[s], err);
+        }
+        __syncwarp();
+    } else if (warp == 9) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+            const uint32_t idesc_s = BF ? IDESC_S_BF16 : IDESC_S_F16;
+            const uint32_t idesc_o = BF ? IDESC_O_BF16 : IDESC_O_F16;
+            const uint32_t sq = smem_u32(smem + SMEM_Q), sk = smem_u32(smem + SMEM_K), sv = smem_u32(smem + SMEM_V),
+                           sp = smem_u32(smem + SMEM_P);
+            auto issue_s = [&](int q, int j) {
+                const int s = j % KV_STAGES;
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ks++)
+                    tc_mma_f16(tmem + q * TK, sw128_desc(sq + q * TILE_BYTES) + 2 * ks,
+                               sw128_desc(sk + s * TILE_BYTES) + 2 * ks, idesc_s, ks != 0);
+                tc_commit(&bar->s_full[q]);
+            };
+            // P: two 64-key K-major atoms of 16 KB, 32 bytes per 16-key step;
+            // V: MN-major, 16 keys (2 KB) per step, 8-key groups 1 KB apart
+            auto issue_o = [&](int q, int j) {
+                const int s = j % KV_STAGES;
+#pragma unroll
+                for (int ks = 0; ks < TK / 16; ks++)
+                    tc_mma_f16(tmem + 2 * TK + q * HD,
+                               sw128_desc(sp + q * P_BYTES + (ks >> 2) * TILE_BYTES) + 2 * (ks & 3),
+                               sw128_desc(sv + s * TILE_BYTES + ks * 2048), idesc_o, ks != 0);
+                tc_commit(&bar->o_full[q]);
+            };
+            bool ok = mbar_wait(&bar->q_full, 0, err, abort_flag);
+            if (ok) ok = mbar_wait(&bar->kv_full[0], 0, err, abort_flag);
+            if (ok) {
+                tc_fence_after();
+                for (int q = 0; q < nq; q++) issue_s(q, 0);
+            }
+            for (int j = 0; j < nkt && ok; j++) {
+                const bool next = j + 1 < nkt;
+                if (next) {
+                    ok = mbar_wait(&bar->kv_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, err, abort_flag);
+                    if (!ok) break;
+                }
+                for (int q = 0; q < nq && ok; q++) {
+                    // softmax of tile j has read S_q and written P_q: S_q(j+1) and P_q V_j can go
+                    ok = mbar_wait(&bar->p_full[q], j & 1, err, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (next) issue_s(q, j + 1);
+                    issue_o(q, j);
+                }
+                if (ok) tc_commit(&bar->kv_empty[j % KV_STAGES]);
+            }
+            // every MMA issued completes before TMEM and shared memory go away
+            tc_commit(&bar->drain);
+            drain_wait(&bar->drain, 0, err);
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------------- softmax
+        const int q = warp >> 2;                 // query tile of this warpgroup
+        const int quarter = warp & 3;            // TMEM lanes this warp may read
+        const int row = quarter * 32 + lane;     // query row in the tile
+        const int qi = q0 + q * TQ + row;        // query row in the sequence
+        const uint32_t t_s = tmem + ((uint32_t)(quarter * 32) << 16) + q * TK;
+        const uint32_t t_o = tmem + ((uint32_t)(quarter * 32) << 16) + 2 * TK + q * HD;
+        uint8_t* prow = smem + SMEM_P + q * P_BYTES + row * 128;
+        const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+        float o[HD];
+#pragma unroll
+        for (int i = 0; i < HD; i++) o[i] = 0.f;
+        float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+        bool ok = q < nq;
+        for (int j = 0; j < nkt && ok; j++) {
+            int w = 1;
+            if (lane == 0) w = mbar_wait(&bar->s_full[q], j & 1, err, abort_flag);
+            ok = __shfl_sync(0xffffffffu, w, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const int kend = L - j * TK;    // keys of this tile inside the sequence (>= 1)
+            const bool whole = kend >= TK;  // only the sequence's last tile is masked
+            // pass 1: the row maximum of this tile
+            float mx = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < TK; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(t_s + c, r);
+                tc_wait_ld();
+                float t[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float a = whole || c + 2 * i < kend ? __uint_as_float(r[2 * i]) : -INFINITY;
+                    const float b = whole || c + 2 * i + 1 < kend ? __uint_as_float(r[2 * i + 1]) : -INFINITY;
+                    t[i] = fmaxf(a, b);
+                }
+#pragma unroll
+                for (int w2 = 8; w2 > 0; w2 >>= 1)
+#pragma unroll
+                    for (int i = 0; i < w2; i++) t[i] = fmaxf(t[i], t[i + w2]);
+                mx = fmaxf(mx, t[0]);
+            }
+            const float mn = fmaxf(m, mx);
+            const float u = mn * sl2;
+            const float alpha = ex2f(m * sl2 - u);  // 0 on the first tile (m = -inf)
+            m = mn;
+            // O_q of the previous tile is complete once its MMA has been
+            // committed; fold it in with its own rescale factor. This also
+            // frees P_q for this tile.
+            if (j > 0) {
+                if (lane == 0) w = mbar_wait(&bar->o_full[q], (j - 1) & 1, err, abort_flag);
+                ok = __shfl_sync(0xffffffffu, w, 0);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < HD; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_o + c, r);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[c + i] = fmaf(o[c + i], alpha_prev, __uint_as_float(r[i]));
+                }
+            }
+            // pass 2: p, the row sum, and P in the swizzled K-major layout
+            // (key chunk k8 of 8 keys at 16-byte slot k8 ^ (row % 8) of the
+            // row's 128-byte line in swizzle atom k8 / 8)
+            float rs = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < TK; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(t_s + c, r);
+                tc_wait_ld();
+                float p[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    p[i] = whole || c + i < kend ? ex2f(fmaf(__uint_as_float(r[i]), sl2, -u)) : 0.f;
+                float ps[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++) ps[i] = p[2 * i] + p[2 * i + 1];
+#pragma unroll
+                for (int w2 = 8; w2 > 0; w2 >>= 1)
+#pragma unroll
+                    for (int i = 0; i < w2; i++) ps[i] += ps[i + w2];
+                rs += ps[0];
+#pragma unroll
+                for (int k8 = 0; k8 < 4; k8++) {
+                    const int chunk = (c >> 3) + k8;  // 0..15
+                    uint4 v;
+                    v.x = pack16<T>(p[8 * k8 + 0], p[8 * k8 + 1]);
+                    v.y = pack16<T>(p[8 * k8 + 2], p[8 * k8 + 3]);
+                    v.z = pack16<T>(p[8 * k8 + 4], p[8 * k8 + 5]);
+                    v.w = pack16<T>(p[8 * k8 + 6], p[8 * k8 + 7]);
+                    *reinterpret_cast<uint4*>(prow + (chunk >> 3) * TILE_BYTES + (((chunk & 7) ^ (row & 7)) << 4)) = v;
+                }
+            }
+            l = l * alpha + rs;
+            alpha_prev = alpha;
+            // S_q is read and P_q written: hand both to the MMA warp
+            fence_proxy_async();
+            tc_fence_before();
+            mbar_arrive(&bar->p_full[q]);
+        }
+        if (ok) {
+            // the last tile's O_q
+            int w = 1;
+            if (lane == 0) w = mbar_wait(&bar->o_full[q], (nkt - 1) & 1, err, abort_flag);
+            ok = __shfl_sync(0xffffffffu, w, 0);
+            if (ok) {
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < HD; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_o + c, r);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[c + i] = fmaf(o[c + i], alpha_prev, __uint_as_float(r[i]));
+                }
+                if (qi < L) {
+                    const float inv = 1.0f / l;
+                    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)(start + qi) * D + h * HD);
+#pragma unroll
+                    for (int c = 0; c < HD / 8; c++) {
+                        uint4 v;
+                        v.x = pack16<T>(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+                        v.y = pack16<T>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+                        v.z = pack16<T>(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+                        v.w = pack16<T>(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+                        dst[c] = v;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 9) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace
+
+cudaError_t launch_attention_tc(bool bf16, const CUtensorMap& qkv_map, void* out, const int* cu_seqlens, int n_seqs,
+                                int M, int max_len, int min_len, int* err, cudaStream_t stream) {
+    if (n_seqs <= 0 || max_len < min_len) return cudaSuccess;
+    dim3 grid((max_len + NQT * TQ - 1) / (NQT * TQ), H, n_seqs);
+    if (bf16)
+        return launch_k(attention_tc_kernel<__nv_bfloat16>, grid, TC_THREADS, SMEM_TC, stream, qkv_map,
+                        static_cast<__nv_bfloat16*>(out), cu_seqlens, M, max_len, min_len, err);
+    return launch_k(attention_tc_kernel<__half>, grid, TC_THREADS, SMEM_TC, stream, qkv_map,
+                    static_cast<__half*>(out), cu_seqlens, M, max_len, min_len, err);
+}
+
+cudaError_t attention_tc_prepare() {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<__nv_bfloat16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attention_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
+    return e;
+}
+
+}  // namespace laya

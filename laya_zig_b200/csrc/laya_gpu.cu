@@ -263,6 +263,7 @@ struct Outs {
 struct ActMaps {
     CUtensorMap a_xn, a_ctx, a_mlp, a_ff;  // A operands, box 128 x 64
     CUtensorMap o_qkv, o_mlp, o_ff, o_x;   // outputs, box 32 rows x 128 bytes
+    CUtensorMap a_qkv;                     // tcgen05 attention's Q, K, V boxes, 128 x 64
 };
 
 int build_maps(laya_ctx* c, int M, ActMaps* m) {
@@ -274,6 +275,7 @@ int build_maps(laya_ctx* c, int M, ActMaps* m) {
     if (r == CUDA_SUCCESS) r = make_out_map(&m->o_mlp, c->mlp, INTER, M, 2, c->bf16);
     if (r == CUDA_SUCCESS) r = make_out_map(&m->o_ff, c->ff, HEAD_FF, M, 2, c->bf16);
     if (r == CUDA_SUCCESS) r = make_out_map(&m->o_x, c->x, D, M, 4, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&m->a_qkv, c->qkv, 3 * D, M, 128, c->bf16);
     if (r != CUDA_SUCCESS) return fail(c, LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return LAYA_OK;
 }
@@ -290,6 +292,20 @@ cudaError_t gemm(laya_ctx* c, int epi, const CUtensorMap& a, const CUtensorMap& 
     g.rope_cols = rope_cols;
     g.err = c->d_err;
     return launch_gemm(epi, 256, c->bf16, a, b, out, g, c->num_sms, s);
+}
+
+// One attention layer. Global layers hand sequences of at least
+// attention_tc_min_len() tokens to the tcgen05 kernel and the rest to the
+// mma.sync kernel (per sequence, so a sequence's result does not depend on
+// the batch it is in); sliding layers run the mma.sync kernel.
+cudaError_t attention(laya_ctx* c, const Batch& b, const ActMaps& am, int window, cudaStream_t s) {
+    const int tc_len = attention_tc_min_len();
+    const bool tc = window < 0 && b.maxlen >= tc_len;
+    cudaError_t e = launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.M, b.maxlen, window, c->d_err, s,
+                                     tc ? tc_len : 0x7fffffff);
+    if (e == cudaSuccess && tc)
+        e = launch_attention_tc(c->bf16, am.a_qkv, c->ctxb, b.cu, b.S, b.M, b.maxlen, tc_len, c->d_err, s);
+    return e;
 }
 
 // The whole forward on stream `s`. The hook sees begin(stage)/end(stage)
@@ -321,8 +337,7 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
         if (w.attn_norm) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.attn_norm, nullptr, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_QKV,
             gemm(c, EPI_QKV, am.a_xn, w.m_qkv, am.o_qkv, M, 3 * D, D, nullptr, 2 * D, s));
-        RUN(LAYA_STAGE_ATTN, launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, M, b.maxlen,
-                                              (l % 3) ? WINDOW : -1, c->d_err, s));
+        RUN(LAYA_STAGE_ATTN, attention(c, b, am, (l % 3) ? WINDOW : -1, s));
         RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_wo, am.o_x, M, D, D, nullptr, 0, s));
         RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.mlp_norm, nullptr, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_UP,
@@ -339,8 +354,7 @@ cudaError_t run_forward(laya_ctx* c, const Batch& b, const Outs& o, const ActMap
         const HeadW& w = c->head[l];
         if (l > 0) RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n1w, w.n1b, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_QKV, gemm(c, EPI_QKV, am.a_xn, w.m_in, am.o_qkv, M, 3 * D, D, w.in_b, 0, s));
-        RUN(LAYA_STAGE_ATTN,
-            launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, M, b.maxlen, -1, c->d_err, s));
+        RUN(LAYA_STAGE_ATTN, attention(c, b, am, -1, s));
         RUN(LAYA_STAGE_GEMM_OUT, gemm(c, EPI_RESID, am.a_ctx, w.m_out, am.o_x, M, D, D, w.out_b, 0, s));
         RUN(LAYA_STAGE_NORM, launch_ln(c->bf16, c->x, c->xn, w.n2w, w.n2b, M, c->num_sms, s));
         RUN(LAYA_STAGE_GEMM_UP,
