@@ -460,7 +460,7 @@ def run_long(args):
     torch.cuda.set_device(0)
     weights = synth.make_weights(0)
     model = gpu.LayaGPU.from_bf16(weights, device=0, precision=args.precision)
-    d = synth.long_decision(8192, 16, seed=3)
+    d = synth.long_decision(args.long_len, 16, seed=3)
     p = gpu.pack([d])
     dev = {k: torch.from_numpy(v.view(np.int32)).cuda() for k, v in p.items() if k != "max_len"}
     M, G = len(p["ids"]), int(p["cu_markers"][-1])
@@ -510,12 +510,12 @@ def run_long(args):
     assert np.isfinite(a).all() and abs(a.sum() - 1) < 1e-4
     h2d = 4 * M + 4 * 2 + 4 + 4 * G + 4 * 2
     print(json.dumps({
-        "metric": "long-context decision latency (1 x 8192 tokens, 16 markers)", "value": 1e3 / ms,
+        "metric": "long-context decision latency (1 x %d tokens, 16 markers)" % M, "value": 1e3 / ms,
         "unit": "decisions/s", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
         "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": args.precision,
         "data": "synthetic (seeded weights and token ids)",
-        "config": {"workload": "one decision of 8192 tokens, 16 markers at random positions, global attention "
-                               "every third layer, sliding window 128 elsewhere",
+        "config": {"workload": "one decision of %d tokens, 16 markers at random positions, global attention "
+                               "every third layer, sliding window 128 elsewhere" % M,
                    "l2": "flushed between timed steps"},
         "latency_ms": ms, "roofline": rl[0] if rl else None, "rooflines": rl,
         "whole_step_tflops": (g_fl + s_fl + gemm_fl) / (ms / 1e3) / 1e12,
@@ -540,6 +540,7 @@ def main():
                     help="snake: the 64 x 180 headline batch (default); sweep: the bucketed throughput sweep; "
                          "gemm: isolated projection GEMMs; long: one 8192-token decision")
     ap.add_argument("--sweep-n", type=int, default=65536)
+    ap.add_argument("--long-len", type=int, default=8192, help="--workload long: the sequence length")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":

@@ -8,23 +8,27 @@
 //   warp 8      TMA producer: both Q tiles once, then K_j and V_j (128 x 64
 //               16-bit boxes, 128-byte swizzle) into a KV_STAGES-deep ring.
 //   warp 9      TMEM owner and MMA issuer: S_q = Q_q K_j^T (M 128, N 128,
-//               K 64) into TMEM, then O_q = P_q V_j (M 128, N 64, K 128)
-//               with P from shared memory and V read MN-major.
+//               K 64) into TMEM, then O_q += P_q V_j (M 128, N 64, K 128)
+//               accumulated in TMEM across key tiles, with P from shared
+//               memory and V read MN-major.
 //   warps 0-7   two softmax warpgroups, one per query tile; thread t of a
-//               group owns query row t (its TMEM lane). Per key tile: the
-//               row maximum (first pass over S), the previous tile's O_q
-//               folded into the register accumulator with its rescale
-//               factor, then p = 2^(s*log2(e)/8 - m*log2(e)/8) with the row
-//               sum in f32 and P rounded to 16 bits into shared memory in the
-//               K-major swizzled layout the MMA reads (second pass).
+//               group owns query row t (its TMEM lane). Per key tile it
+//               copies its 128 scores from TMEM to registers (S_q is then
+//               free for the next tile's MMA), takes the row maximum, and
+//               writes p = 2^(s*log2(e)/8 - m*log2(e)/8) rounded to 16 bits
+//               into one of two P buffers (K-major swizzled, as the MMA
+//               reads it), keeping the row sum in f32.
 //
-// The softmax is the online form of the mma.sync kernel (attention.cu): same
-// scale, same exp2 argument, normalised once at the end as the reference
-// does (2479-2486); only the MMA shapes and so the summation order differ.
-// Keys past the sequence end are masked to -inf; query rows past it are
-// computed and not stored. Every wait is bounded (common.cuh): a CTA that
-// gives up sets the error word, drains its own TMA loads and MMAs, frees
-// TMEM and exits.
+// The reference point m of a row moves only when the row's maximum grows by
+// more than 8 in the exponent (p then stays below 2^8): the warp rescales
+// its rows of the TMEM accumulator and the row sum by 2^(m_old - m_new)
+// before the next P.V accumulates. Softmax is invariant to the reference
+// point, so the result is that of the online softmax of the mma.sync
+// kernel (attention.cu: same scale, same exp2 argument, normalised once at
+// the end as the reference does, 2479-2486) up to rounding. Keys past the
+// sequence end are masked to -inf; query rows past it are computed and not
+// stored. Every wait is bounded (common.cuh): a CTA that gives up sets the
+// error word, drains its own TMA loads and MMAs, frees TMEM and exits.
 #include <type_traits>
 
 #include "attention.cuh"
@@ -35,7 +39,7 @@ namespace {
 constexpr int TQ = 128;        // query rows per tile (one TMEM lane each)
 constexpr int TK = 128;        // keys per tile
 constexpr int NQT = 2;         // query tiles per CTA
-constexpr int KV_STAGES = 3;
+constexpr int KV_STAGES = 2;
 constexpr int TC_THREADS = 320;
 constexpr int TILE_BYTES = TQ * HD * 2;            // 16 KB: a 128 x 64 16-bit box
 constexpr int P_BYTES = TQ * TK * 2;               // 32 KB: 128 x 128 16-bit, two 64-key swizzle atoms
@@ -43,7 +47,7 @@ constexpr int SMEM_Q = 0;
 constexpr int SMEM_K = SMEM_Q + NQT * TILE_BYTES;
 constexpr int SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_P = SMEM_V + KV_STAGES * TILE_BYTES;
-constexpr int SMEM_BAR = SMEM_P + NQT * P_BYTES;
+constexpr int SMEM_BAR = SMEM_P + 2 * NQT * P_BYTES;  // two P buffers per query tile
 constexpr int SMEM_TC = SMEM_BAR + 256 + 1024;     // barriers, TMEM slot, 1 KB alignment slack
 constexpr uint32_t TMEM_COLS = 512;                // S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
 constexpr uint32_t IDESC_S_BF16 = idesc_f16(TQ, TK, true);
@@ -55,7 +59,7 @@ constexpr uint32_t IDESC_O_F16 = idesc_f16(TQ, HD, false) | (1u << 16);
 struct Bars {
     uint64_t q_full;
     uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
-    uint64_t s_full[NQT], p_full[NQT], o_full[NQT];
+    uint64_t s_full[NQT], s_free[NQT], p_full[NQT], o_full[NQT], p_free[NQT][2];
     uint64_t drain;
     uint32_t tmem;
     int abort;
@@ -121,8 +125,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int q = 0; q < NQT; q++) {
             mbar_init(&bar->s_full[q], 1);
+            mbar_init(&bar->s_free[q], TQ);
             mbar_init(&bar->p_full[q], TQ);
             mbar_init(&bar->o_full[q], 1);
+            mbar_init(&bar->p_free[q][0], 1);
+            mbar_init(&bar->p_free[q][1], 1);
         }
         mbar_init(&bar->drain, 1);
         bar->abort = 0;
@@ -185,12 +192,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // V: MN-major, 16 keys (2 KB) per step, 8-key groups 1 KB apart
             auto issue_o = [&](int q, int j) {
                 const int s = j % KV_STAGES;
+                const uint32_t pb = sp + (q * 2 + (j & 1)) * P_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < TK / 16; ks++)
-                    tc_mma_f16(tmem + 2 * TK + q * HD,
-                               sw128_desc(sp + q * P_BYTES + (ks >> 2) * TILE_BYTES) + 2 * (ks & 3),
-                               sw128_desc(sv + s * TILE_BYTES + ks * 2048), idesc_o, ks != 0);
+                    tc_mma_f16(tmem + 2 * TK + q * HD, sw128_desc(pb + (ks >> 2) * TILE_BYTES) + 2 * (ks & 3),
+                               sw128_desc(sv + s * TILE_BYTES + ks * 2048), idesc_o, (j | ks) != 0);
                 tc_commit(&bar->o_full[q]);
+                tc_commit(&bar->p_free[q][j & 1]);
             };
             bool ok = mbar_wait(&bar->q_full, 0, err, abort_flag);
             if (ok) ok = mbar_wait(&bar->kv_full[0], 0, err, abort_flag);
@@ -199,18 +207,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int q = 0; q < nq; q++) issue_s(q, 0);
             }
             for (int j = 0; j < nkt && ok; j++) {
-                const bool next = j + 1 < nkt;
-                if (next) {
+                // S_q(j+1) as soon as the softmax has copied S_q(j) out of
+                // TMEM, then P_q V_j once it has written P_q(j)
+                if (j + 1 < nkt) {
                     ok = mbar_wait(&bar->kv_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, err, abort_flag);
-                    if (!ok) break;
+                    for (int q = 0; q < nq && ok; q++) {
+                        ok = mbar_wait(&bar->s_free[q], j & 1, err, abort_flag);
+                        if (ok) {
+                            tc_fence_after();
+                            issue_s(q, j + 1);
+                        }
+                    }
                 }
                 for (int q = 0; q < nq && ok; q++) {
-                    // softmax of tile j has read S_q and written P_q: S_q(j+1) and P_q V_j can go
                     ok = mbar_wait(&bar->p_full[q], j & 1, err, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    if (next) issue_s(q, j + 1);
-                    issue_o(q, j);
+                    if (ok) {
+                        tc_fence_after();
+                        issue_o(q, j);
+                    }
                 }
                 if (ok) tc_commit(&bar->kv_empty[j % KV_STAGES]);
             }
@@ -227,12 +241,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int qi = q0 + q * TQ + row;        // query row in the sequence
         const uint32_t t_s = tmem + ((uint32_t)(quarter * 32) << 16) + q * TK;
         const uint32_t t_o = tmem + ((uint32_t)(quarter * 32) << 16) + 2 * TK + q * HD;
-        uint8_t* prow = smem + SMEM_P + q * P_BYTES + row * 128;
         const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
-        float o[HD];
-#pragma unroll
-        for (int i = 0; i < HD; i++) o[i] = 0.f;
-        float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+        constexpr float RESCALE = 8.0f;                  // exponent growth that moves the reference point
+        float m = -INFINITY, l = 0.f;
         bool ok = q < nq;
         for (int j = 0; j < nkt && ok; j++) {
             int w = 1;
@@ -240,36 +251,70 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = __shfl_sync(0xffffffffu, w, 0);
             if (!ok) break;
             tc_fence_after();
-            const int kend = L - j * TK;    // keys of this tile inside the sequence (>= 1)
-            const bool whole = kend >= TK;  // only the sequence's last tile is masked
-            // pass 1: the row maximum of this tile
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < TK; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(t_s + c, r);
-                tc_wait_ld();
-                float t[16];
+            float sv[TK];
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const float a = whole || c + 2 * i < kend ? __uint_as_float(r[2 * i]) : -INFINITY;
-                    const float b = whole || c + 2 * i + 1 < kend ? __uint_as_float(r[2 * i + 1]) : -INFINITY;
-                    t[i] = fmaxf(a, b);
-                }
+            for (int c = 0; c < TK; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
+            tc_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&bar->s_free[q]);  // S_q may be overwritten by the next tile's MMA
+            const int kend = L - j * TK;   // keys of this tile inside the sequence (>= 1)
+            if (kend < TK) {               // only the sequence's last tile is masked
 #pragma unroll
-                for (int w2 = 8; w2 > 0; w2 >>= 1)
-#pragma unroll
-                    for (int i = 0; i < w2; i++) t[i] = fmaxf(t[i], t[i + w2]);
-                mx = fmaxf(mx, t[0]);
+                for (int i = 0; i < TK; i++)
+                    if (i >= kend) sv[i] = -INFINITY;
             }
-            const float mn = fmaxf(m, mx);
-            const float u = mn * sl2;
-            const float alpha = ex2f(m * sl2 - u);  // 0 on the first tile (m = -inf)
-            m = mn;
-            // O_q of the previous tile is complete once its MMA has been
-            // committed; fold it in with its own rescale factor. This also
-            // frees P_q for this tile.
-            if (j > 0) {
+            float t[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) t[i] = fmaxf(sv[i], sv[i + 8]);
+#pragma unroll
+            for (int i = 16; i < TK; i += 8)
+#pragma unroll
+                for (int k = 0; k < 8; k++) t[k] = fmaxf(t[k], sv[i + k]);
+            const float mx = fmaxf(fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3])), fmaxf(fmaxf(t[4], t[5]), fmaxf(t[6], t[7])));
+            // move the reference point when the maximum grew by more than
+            // RESCALE in the exponent (always on the first tile); the warp
+            // rescales its rows of O together (TMEM access is per warp),
+            // after P is written, when fewer registers are live
+            const bool need = (mx - m) * sl2 > RESCALE;
+            float alpha = 1.0f;
+            if (j == 0) {
+                m = mx;
+            } else if (need) {
+                alpha = ex2f((m - mx) * sl2);
+                m = mx;
+                l *= alpha;
+            }
+            const bool rescale = j > 0 && __any_sync(0xffffffffu, need);
+            const float u = m * sl2;
+            // P_q(j) goes to buffer j % 2, free once P_q(j-2) V has completed
+            if (j >= 2) {
+                if (lane == 0) w = mbar_wait(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag);
+                ok = __shfl_sync(0xffffffffu, w, 0);
+                if (!ok) break;
+            }
+            // p for 8 keys at a time, summed into 8 partial sums, rounded and
+            // stored: key chunk k8 of 8 keys goes to 16-byte slot
+            // (k8 % 8) ^ (row % 8) of the row's 128-byte line in swizzle atom k8 / 8
+            uint8_t* prow = smem + SMEM_P + (q * 2 + (j & 1)) * P_BYTES + row * 128;
+            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int k8 = 0; k8 < TK / 8; k8++) {
+                float p[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    p[k] = ex2f(fmaf(sv[8 * k8 + k], sl2, -u));
+                    ps[k] += p[k];
+                }
+                uint4 v;
+                v.x = pack16<T>(p[0], p[1]);
+                v.y = pack16<T>(p[2], p[3]);
+                v.z = pack16<T>(p[4], p[5]);
+                v.w = pack16<T>(p[6], p[7]);
+                *reinterpret_cast<uint4*>(prow + (k8 >> 3) * TILE_BYTES + (((k8 & 7) ^ (row & 7)) << 4)) = v;
+            }
+            l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            if (rescale) {
+                // O_q holds P V up to tile j-1 once that MMA has completed
                 if (lane == 0) w = mbar_wait(&bar->o_full[q], (j - 1) & 1, err, abort_flag);
                 ok = __shfl_sync(0xffffffffu, w, 0);
                 if (!ok) break;
@@ -280,63 +325,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     tmem_ld32(t_o + c, r);
                     tc_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[c + i] = fmaf(o[c + i], alpha_prev, __uint_as_float(r[i]));
+                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                    tmem_st32(t_o + c, r);
                 }
+                tc_wait_st();
             }
-            // pass 2: p, the row sum, and P in the swizzled K-major layout
-            // (key chunk k8 of 8 keys at 16-byte slot k8 ^ (row % 8) of the
-            // row's 128-byte line in swizzle atom k8 / 8)
-            float rs = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < TK; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(t_s + c, r);
-                tc_wait_ld();
-                float p[32];
-#pragma unroll
-                for (int i = 0; i < 32; i++)
-                    p[i] = whole || c + i < kend ? ex2f(fmaf(__uint_as_float(r[i]), sl2, -u)) : 0.f;
-                float ps[16];
-#pragma unroll
-                for (int i = 0; i < 16; i++) ps[i] = p[2 * i] + p[2 * i + 1];
-#pragma unroll
-                for (int w2 = 8; w2 > 0; w2 >>= 1)
-#pragma unroll
-                    for (int i = 0; i < w2; i++) ps[i] += ps[i + w2];
-                rs += ps[0];
-#pragma unroll
-                for (int k8 = 0; k8 < 4; k8++) {
-                    const int chunk = (c >> 3) + k8;  // 0..15
-                    uint4 v;
-                    v.x = pack16<T>(p[8 * k8 + 0], p[8 * k8 + 1]);
-                    v.y = pack16<T>(p[8 * k8 + 2], p[8 * k8 + 3]);
-                    v.z = pack16<T>(p[8 * k8 + 4], p[8 * k8 + 5]);
-                    v.w = pack16<T>(p[8 * k8 + 6], p[8 * k8 + 7]);
-                    *reinterpret_cast<uint4*>(prow + (chunk >> 3) * TILE_BYTES + (((chunk & 7) ^ (row & 7)) << 4)) = v;
-                }
-            }
-            l = l * alpha + rs;
-            alpha_prev = alpha;
-            // S_q is read and P_q written: hand both to the MMA warp
             fence_proxy_async();
+            // Hand P_q(j) over only once P_q(j-1) V has completed: the MMA
+            // warp has then taken p_full's previous phase, so the barrier is
+            // never two phases ahead of its waiter.
+            if (j >= 1) {
+                if (lane == 0) w = mbar_wait(&bar->p_free[q][(j - 1) & 1], ((j - 1) >> 1) & 1, err, abort_flag);
+                ok = __shfl_sync(0xffffffffu, w, 0);
+                if (!ok) break;
+            }
             tc_fence_before();
             mbar_arrive(&bar->p_full[q]);
         }
         if (ok) {
-            // the last tile's O_q
+            // O_q is complete once the last P V has
             int w = 1;
             if (lane == 0) w = mbar_wait(&bar->o_full[q], (nkt - 1) & 1, err, abort_flag);
             ok = __shfl_sync(0xffffffffu, w, 0);
             if (ok) {
                 tc_fence_after();
+                float o[HD];
 #pragma unroll
-                for (int c = 0; c < HD; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_o + c, r);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; i++) o[c + i] = fmaf(o[c + i], alpha_prev, __uint_as_float(r[i]));
-                }
+                for (int c = 0; c < HD; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
+                tc_wait_ld();
                 if (qi < L) {
                     const float inv = 1.0f / l;
                     uint4* dst = reinterpret_cast<uint4*>(out + (size_t)(start + qi) * D + h * HD);

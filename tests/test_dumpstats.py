@@ -21,7 +21,10 @@ same 1e-3 relative to max(1, |sum|), a bar set for the reference's f32
 activations; the sum of L x 768 values cancels to a few units while its
 terms carry the 16-bit rounding of tensor-core operands (about 1e-3 each,
 so the sum moves by ~sqrt(L x 768) x 1e-3 = 0.2 at L = 64). The sum is
-therefore held to 1e-3 of the abs-sum, the scale of its terms.
+therefore held to 1e-3 of the abs-sum, the scale of its terms. In the bf16
+mode the first three values (single elements of the state, of magnitude
+0.5-2) carry the bf16 operands' rounding, measured up to 7e-3 at the head
+layers; they are held to 1e-2 there and to refcheck's 5e-3 in the f16 mode.
 """
 import importlib.util
 import os
@@ -161,7 +164,7 @@ def test_gpu_dump_against_refcheck_goldens(name, precision, weights, gpu_model):
     worst = {}
     for t in TAGS:
         ref = g["tags"][t]
-        ok, err = refcheck_compare(layers[t], (ref[:3], ref[3], ref[4]))
+        ok, err = refcheck_compare(layers[t], (ref[:3], ref[3], ref[4]), tol=1e-2 if precision == "bf16" else 5e-3)
         worst[t] = err
         assert ok, (precision, name, t, err)
     if g["logits"]:
