@@ -72,6 +72,25 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
+// 2^x on the FMA pipe, for part of the softmax's exponentials (the SFU that
+// ex2.approx uses is the busiest unit of this kernel). Range reduction to
+// the nearest integer n as in the reference's expv (src/main.zig:598-615),
+// here by adding and subtracting 1.5 * 2^23; 2^f for |f| <= 1/2 by its
+// Taylor series in f ln 2 to degree 4 (relative error below 6e-5, under the
+// 16-bit rounding P gets); n added to the exponent field. x is clamped at
+// -125 (2^-125 ~ 2e-38 for masked keys, nothing next to a row sum >= 1).
+__device__ __forceinline__ float ex2_fma(float x) {
+    x = fmaxf(x, -125.0f);
+    const float t = x + 12582912.0f;
+    const float f = x - (t - 12582912.0f);
+    float p = 9.618129107628477e-3f;           // ln2^4 / 24
+    p = fmaf(p, f, 5.550410866482158e-2f);     // ln2^3 / 6
+    p = fmaf(p, f, 2.402265069591007e-1f);     // ln2^2 / 2
+    p = fmaf(p, f, 6.931471805599453e-1f);     // ln2
+    p = fmaf(p, f, 1.0f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack16(float a, float b);
 template <>
@@ -159,7 +178,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int j = 0; j < nkt && !*abort_flag; j++) {
                 const int s = j % KV_STAGES;
                 const uint32_t ph = (j / KV_STAGES) & 1;
-                if (!mbar_wait(&bar->kv_empty[s], ph ^ 1, err, abort_flag)) break;
+                if (!mbar_wait_sleep(&bar->kv_empty[s], ph ^ 1, err, abort_flag)) break;
                 mbar_arrive_expect_tx(&bar->kv_full[s], 2 * TILE_BYTES);
                 tma_load_2d(smem + SMEM_K + s * TILE_BYTES, &qkv_map, &bar->kv_full[s], D + h * HD, start + j * TK);
                 tma_load_2d(smem + SMEM_V + s * TILE_BYTES, &qkv_map, &bar->kv_full[s], 2 * D + h * HD,
@@ -200,8 +219,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc_commit(&bar->o_full[q]);
                 tc_commit(&bar->p_free[q][j & 1]);
             };
-            bool ok = mbar_wait(&bar->q_full, 0, err, abort_flag);
-            if (ok) ok = mbar_wait(&bar->kv_full[0], 0, err, abort_flag);
+            bool ok = mbar_wait_sleep(&bar->q_full, 0, err, abort_flag);
+            if (ok) ok = mbar_wait_sleep(&bar->kv_full[0], 0, err, abort_flag);
             if (ok) {
                 tc_fence_after();
                 for (int q = 0; q < nq; q++) issue_s(q, 0);
@@ -210,9 +229,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 // S_q(j+1) as soon as the softmax has copied S_q(j) out of
                 // TMEM, then P_q V_j once it has written P_q(j)
                 if (j + 1 < nkt) {
-                    ok = mbar_wait(&bar->kv_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, err, abort_flag);
+                    ok = mbar_wait_sleep(&bar->kv_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, err, abort_flag);
                     for (int q = 0; q < nq && ok; q++) {
-                        ok = mbar_wait(&bar->s_free[q], j & 1, err, abort_flag);
+                        ok = mbar_wait_sleep(&bar->s_free[q], j & 1, err, abort_flag);
                         if (ok) {
                             tc_fence_after();
                             issue_s(q, j + 1);
@@ -220,7 +239,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
                 for (int q = 0; q < nq && ok; q++) {
-                    ok = mbar_wait(&bar->p_full[q], j & 1, err, abort_flag);
+                    ok = mbar_wait_sleep(&bar->p_full[q], j & 1, err, abort_flag);
                     if (ok) {
                         tc_fence_after();
                         issue_o(q, j);
@@ -246,9 +265,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         float m = -INFINITY, l = 0.f;
         bool ok = q < nq;
         for (int j = 0; j < nkt && ok; j++) {
-            int w = 1;
-            if (lane == 0) w = mbar_wait(&bar->s_full[q], j & 1, err, abort_flag);
-            ok = __shfl_sync(0xffffffffu, w, 0);
+            ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar->s_full[q], j & 1, err, abort_flag));
             if (!ok) break;
             tc_fence_after();
             float sv[TK];
@@ -288,8 +305,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const float u = m * sl2;
             // P_q(j) goes to buffer j % 2, free once P_q(j-2) V has completed
             if (j >= 2) {
-                if (lane == 0) w = mbar_wait(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag);
-                ok = __shfl_sync(0xffffffffu, w, 0);
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait_sleep(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag));
                 if (!ok) break;
             }
             // p for 8 keys at a time, summed into 8 partial sums, rounded and
@@ -301,8 +318,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int k8 = 0; k8 < TK / 8; k8++) {
                 float p[8];
 #pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    p[k] = ex2f(fmaf(sv[8 * k8 + k], sl2, -u));
+                for (int k = 0; k < 8; k++) {  // half on the SFU, half on the FMA pipe
+                    const float a = fmaf(sv[8 * k8 + k], sl2, -u);
+                    p[k] = k < 4 ? ex2f(a) : ex2_fma(a);
                     ps[k] += p[k];
                 }
                 uint4 v;
@@ -315,8 +333,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             if (rescale) {
                 // O_q holds P V up to tile j-1 once that MMA has completed
-                if (lane == 0) w = mbar_wait(&bar->o_full[q], (j - 1) & 1, err, abort_flag);
-                ok = __shfl_sync(0xffffffffu, w, 0);
+                ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar->o_full[q], (j - 1) & 1, err, abort_flag));
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
@@ -335,8 +352,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // warp has then taken p_full's previous phase, so the barrier is
             // never two phases ahead of its waiter.
             if (j >= 1) {
-                if (lane == 0) w = mbar_wait(&bar->p_free[q][(j - 1) & 1], ((j - 1) >> 1) & 1, err, abort_flag);
-                ok = __shfl_sync(0xffffffffu, w, 0);
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait_sleep(&bar->p_free[q][(j - 1) & 1], ((j - 1) >> 1) & 1, err, abort_flag));
                 if (!ok) break;
             }
             tc_fence_before();
@@ -344,9 +361,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         if (ok) {
             // O_q is complete once the last P V has
-            int w = 1;
-            if (lane == 0) w = mbar_wait(&bar->o_full[q], (nkt - 1) & 1, err, abort_flag);
-            ok = __shfl_sync(0xffffffffu, w, 0);
+            ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar->o_full[q], (nkt - 1) & 1, err, abort_flag));
             if (ok) {
                 tc_fence_after();
                 float o[HD];
