@@ -5,19 +5,23 @@
 // 128-row query tiles of one head of one sequence and streams the
 // sequence's keys and values through shared memory in tiles of 128:
 //
-//   warp 8      TMA producer: both Q tiles once, then K_j and V_j (128 x 64
+//   warp 16     TMA producer: both Q tiles once, then K_j and V_j (128 x 64
 //               16-bit boxes, 128-byte swizzle) into a KV_STAGES-deep ring.
-//   warp 9      TMEM owner and MMA issuer: S_q = Q_q K_j^T (M 128, N 128,
+//   warp 17     TMEM owner and MMA issuer: S_q = Q_q K_j^T (M 128, N 128,
 //               K 64) into TMEM, then O_q += P_q V_j (M 128, N 64, K 128)
 //               accumulated in TMEM across key tiles, with P from shared
 //               memory and V read MN-major.
-//   warps 0-7   two softmax warpgroups, one per query tile; thread t of a
-//               group owns query row t (its TMEM lane). Per key tile it
-//               copies its 128 scores from TMEM to registers (S_q is then
-//               free for the next tile's MMA), takes the row maximum, and
-//               writes p = 2^(s*log2(e)/8 - m*log2(e)/8) rounded to 16 bits
-//               into one of two P buffers (K-major swizzled, as the MMA
-//               reads it), keeping the row sum in f32.
+//   warps 0-15  softmax, eight warps per query tile: warps w and w + 4 of a
+//               tile's eight read the same TMEM lane quarter (query rows),
+//               the first the tile's keys 0-63, the second keys 64-127, so
+//               each thread holds half a row. Per key tile a thread copies
+//               its 64 scores from TMEM to registers (S_q is then free for
+//               the next tile's MMA), takes their maximum, exchanges it with
+//               its row's other half through shared memory, and writes
+//               p = 2^(s*log2(e)/8 - m*log2(e)/8) rounded to 16 bits into
+//               one of two P buffers (K-major swizzled, as the MMA reads it),
+//               keeping its half of the row sum in f32. Four softmax warps
+//               per scheduler hide each other's latencies.
 //
 // The reference point m of a row moves only when the row's maximum grows by
 // more than 8 in the exponent (p then stays below 2^8): the warp rescales
@@ -40,7 +44,8 @@ constexpr int TQ = 128;        // query rows per tile (one TMEM lane each)
 constexpr int TK = 128;        // keys per tile
 constexpr int NQT = 2;         // query tiles per CTA
 constexpr int KV_STAGES = 2;
-constexpr int TC_THREADS = 320;
+constexpr int TC_THREADS = 576;  // 16 softmax warps, producer, MMA issuer
+constexpr int SM_THREADS = 256;  // softmax threads per query tile
 constexpr int TILE_BYTES = TQ * HD * 2;            // 16 KB: a 128 x 64 16-bit box
 constexpr int P_BYTES = TQ * TK * 2;               // 32 KB: 128 x 128 16-bit, two 64-key swizzle atoms
 constexpr int SMEM_Q = 0;
@@ -49,7 +54,11 @@ constexpr int SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_P = SMEM_V + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_BAR = SMEM_P + 2 * NQT * P_BYTES;  // two P buffers per query tile
 constexpr int SMEM_TC = SMEM_BAR + 256 + 1024;     // barriers, TMEM slot, 1 KB alignment slack
-constexpr uint32_t TMEM_COLS = 512;                // S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
+// TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384), then
+// the row halves' maxima and sums exchanged between the two warps of a lane
+// quarter at 384 + ((parity * 2 + q) * 2 + half)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t X_COL = 384;
 constexpr uint32_t IDESC_S_BF16 = idesc_f16(TQ, TK, true);
 constexpr uint32_t IDESC_S_F16 = idesc_f16(TQ, TK, false);
 // P . V: B (= V) is MN-major (head dim contiguous): transpose-B bit 16.
@@ -65,30 +74,23 @@ struct Bars {
     int abort;
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
+static_assert(SMEM_TC <= 227 * 1024, "shared memory");
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// barrier over the 256 softmax threads of query tile q (ids 1 and 2)
+__device__ __forceinline__ void tile_sync(int q) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + q), "n"(SM_THREADS) : "memory");
+}
 
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// 2^x on the FMA pipe, for part of the softmax's exponentials (the SFU that
-// ex2.approx uses is the busiest unit of this kernel). Range reduction to
-// the nearest integer n as in the reference's expv (src/main.zig:598-615),
-// here by adding and subtracting 1.5 * 2^23; 2^f for |f| <= 1/2 by its
-// Taylor series in f ln 2 to degree 4 (relative error below 6e-5, under the
-// 16-bit rounding P gets); n added to the exponent field. x is clamped at
-// -125 (2^-125 ~ 2e-38 for masked keys, nothing next to a row sum >= 1).
-__device__ __forceinline__ float ex2_fma(float x) {
-    x = fmaxf(x, -125.0f);
-    const float t = x + 12582912.0f;
-    const float f = x - (t - 12582912.0f);
-    float p = 9.618129107628477e-3f;           // ln2^4 / 24
-    p = fmaf(p, f, 5.550410866482158e-2f);     // ln2^3 / 6
-    p = fmaf(p, f, 2.402265069591007e-1f);     // ln2^2 / 2
-    p = fmaf(p, f, 6.931471805599453e-1f);     // ln2
-    p = fmaf(p, f, 1.0f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 template <typename T>
@@ -144,8 +146,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int q = 0; q < NQT; q++) {
             mbar_init(&bar->s_full[q], 1);
-            mbar_init(&bar->s_free[q], TQ);
-            mbar_init(&bar->p_full[q], TQ);
+            mbar_init(&bar->s_free[q], SM_THREADS);
+            mbar_init(&bar->p_full[q], SM_THREADS);
             mbar_init(&bar->o_full[q], 1);
             mbar_init(&bar->p_free[q][0], 1);
             mbar_init(&bar->p_free[q][1], 1);
@@ -155,8 +157,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         fence_barrier_init();
         fence_proxy_async();
     }
-    if (warp == 8 && lane == 0) prefetch_tmap(&qkv_map);
-    if (warp == 9) {
+    if (warp == 16 && lane == 0) prefetch_tmap(&qkv_map);
+    if (warp == 17) {
         tmem_alloc(&bar->tmem, TMEM_COLS);
         tmem_relinquish();
     }
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     griddep_launch();
     griddep_wait();  // qkv comes from the preceding projection
 
-    if (warp == 8) {
+    if (warp == 16) {
         // ---------------------------------------------------------- TMA producer
         if (lane == 0) {
             int issued_phase[KV_STAGES];
@@ -178,7 +180,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int j = 0; j < nkt && !*abort_flag; j++) {
                 const int s = j % KV_STAGES;
                 const uint32_t ph = (j / KV_STAGES) & 1;
-                if (!mbar_wait_sleep(&bar->kv_empty[s], ph ^ 1, err, abort_flag)) break;
+                if (!mbar_wait(&bar->kv_empty[s], ph ^ 1, err, abort_flag)) break;
                 mbar_arrive_expect_tx(&bar->kv_full[s], 2 * TILE_BYTES);
                 tma_load_2d(smem + SMEM_K + s * TILE_BYTES, &qkv_map, &bar->kv_full[s], D + h * HD, start + j * TK);
                 tma_load_2d(smem + SMEM_V + s * TILE_BYTES, &qkv_map, &bar->kv_full[s], 2 * D + h * HD,
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (issued_phase[s] >= 0) drain_wait(&bar->kv_full[s], (uint32_t)issued_phase[s], err);
         }
         __syncwarp();
-    } else if (warp == 9) {
+    } else if (warp == 17) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
             constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
@@ -219,8 +221,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc_commit(&bar->o_full[q]);
                 tc_commit(&bar->p_free[q][j & 1]);
             };
-            bool ok = mbar_wait_sleep(&bar->q_full, 0, err, abort_flag);
-            if (ok) ok = mbar_wait_sleep(&bar->kv_full[0], 0, err, abort_flag);
+            bool ok = mbar_wait(&bar->q_full, 0, err, abort_flag);
+            if (ok) ok = mbar_wait(&bar->kv_full[0], 0, err, abort_flag);
             if (ok) {
                 tc_fence_after();
                 for (int q = 0; q < nq; q++) issue_s(q, 0);
@@ -229,9 +231,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 // S_q(j+1) as soon as the softmax has copied S_q(j) out of
                 // TMEM, then P_q V_j once it has written P_q(j)
                 if (j + 1 < nkt) {
-                    ok = mbar_wait_sleep(&bar->kv_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, err, abort_flag);
+                    ok = mbar_wait(&bar->kv_full[(j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, err, abort_flag);
                     for (int q = 0; q < nq && ok; q++) {
-                        ok = mbar_wait_sleep(&bar->s_free[q], j & 1, err, abort_flag);
+                        ok = mbar_wait(&bar->s_free[q], j & 1, err, abort_flag);
                         if (ok) {
                             tc_fence_after();
                             issue_s(q, j + 1);
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
                 for (int q = 0; q < nq && ok; q++) {
-                    ok = mbar_wait_sleep(&bar->p_full[q], j & 1, err, abort_flag);
+                    ok = mbar_wait(&bar->p_full[q], j & 1, err, abort_flag);
                     if (ok) {
                         tc_fence_after();
                         issue_o(q, j);
@@ -254,44 +256,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
     } else {
         // ---------------------------------------------------------- softmax
-        const int q = warp >> 2;                 // query tile of this warpgroup
-        const int quarter = warp & 3;            // TMEM lanes this warp may read
+        const int q = warp >> 3;                 // query tile of this warp
+        const int quarter = warp & 3;            // TMEM lanes (query rows) this warp may read
+        const int half = (warp >> 2) & 1;        // which 64 keys of the tile / 32 columns of O
         const int row = quarter * 32 + lane;     // query row in the tile
         const int qi = q0 + q * TQ + row;        // query row in the sequence
-        const uint32_t t_s = tmem + ((uint32_t)(quarter * 32) << 16) + q * TK;
-        const uint32_t t_o = tmem + ((uint32_t)(quarter * 32) << 16) + 2 * TK + q * HD;
+        const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+        const uint32_t t_s = tmem + lanes + q * TK + half * (TK / 2);
+        const uint32_t t_o = tmem + lanes + 2 * TK + q * HD + half * (HD / 2);
         const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
         constexpr float RESCALE = 8.0f;                  // exponent growth that moves the reference point
+        constexpr int HK = TK / 2;                       // keys per thread per tile
         float m = -INFINITY, l = 0.f;
         bool ok = q < nq;
-        for (int j = 0; j < nkt && ok; j++) {
-            ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar->s_full[q], j & 1, err, abort_flag));
-            if (!ok) break;
-            tc_fence_after();
-            float sv[TK];
+        // Every softmax thread of the tile takes part in each tile_sync below,
+        // also after a failed wait (ok false: it then only keeps the barrier
+        // count), so a thread that gives up never leaves the others waiting.
+        for (int j = 0; j < nkt; j++) {
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->s_full[q], j & 1, err, abort_flag));
+            const int kend = L - j * TK - half * HK;  // keys of this half inside the sequence
+            float mh = -INFINITY;
+            if (ok) {
+                // first read of this half's scores: their maximum
+                float sv[HK];
+                tc_fence_after();
+                tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+                tc_wait_ld();
+                if (kend < HK) {  // only the sequence's last tile is masked
 #pragma unroll
-            for (int c = 0; c < TK; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
-            tc_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&bar->s_free[q]);  // S_q may be overwritten by the next tile's MMA
-            const int kend = L - j * TK;   // keys of this tile inside the sequence (>= 1)
-            if (kend < TK) {               // only the sequence's last tile is masked
+                    for (int i = 0; i < HK; i++)
+                        if (i >= kend) sv[i] = -INFINITY;
+                }
+                float t[8];
 #pragma unroll
-                for (int i = 0; i < TK; i++)
-                    if (i >= kend) sv[i] = -INFINITY;
+                for (int k = 0; k < 8; k++) t[k] = max3f(sv[k], sv[k + 8], sv[k + 16]);
+#pragma unroll
+                for (int i = 24; i < HK; i += 16)
+#pragma unroll
+                    for (int k = 0; k < 8; k++) t[k] = max3f(t[k], sv[i + k], sv[i + 8 + k]);
+                mh = max3f(max3f(t[0], t[1], t[2]), max3f(t[3], t[4], t[5]), fmaxf(t[6], t[7]));
             }
-            float t[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) t[i] = fmaxf(sv[i], sv[i + 8]);
-#pragma unroll
-            for (int i = 16; i < TK; i += 8)
-#pragma unroll
-                for (int k = 0; k < 8; k++) t[k] = fmaxf(t[k], sv[i + k]);
-            const float mx = fmaxf(fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3])), fmaxf(fmaxf(t[4], t[5]), fmaxf(t[6], t[7])));
+            // the row's maximum: this half's and the other half's, through a
+            // TMEM column of the shared lane quarter (columns alternate with
+            // the tile's parity, so one is rewritten only after its reader
+            // passed the next barrier)
+            const uint32_t xc = tmem + lanes + X_COL + (((j & 1) * 2 + q) * 2);
+            tmem_st1(xc + half, __float_as_uint(mh));
+            tc_wait_st();
+            tc_fence_before();
+            tile_sync(q);
+            tc_fence_after();
+            const float mx = fmaxf(mh, __uint_as_float(tmem_ld1(xc + (half ^ 1))));
+            tc_wait_ld();
+            if (!ok) continue;
             // move the reference point when the maximum grew by more than
-            // RESCALE in the exponent (always on the first tile); the warp
-            // rescales its rows of O together (TMEM access is per warp),
-            // after P is written, when fewer registers are live
+            // RESCALE in the exponent (always on the first tile); both halves
+            // of a row decide alike, and a warp rescales its 32 columns of O
+            // for its 32 rows together (TMEM access is per warp)
             const bool need = (mx - m) * sl2 > RESCALE;
             float alpha = 1.0f;
             if (j == 0) {
@@ -303,24 +325,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             const bool rescale = j > 0 && __any_sync(0xffffffffu, need);
             const float u = m * sl2;
+            // second read of the scores (S_q is then free for the next
+            // tile's MMA): p, the row sum and P
+            float sv[HK];
+            tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+            tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+            tc_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&bar->s_free[q]);
+            if (kend < HK) {
+#pragma unroll
+                for (int i = 0; i < HK; i++)
+                    if (i >= kend) sv[i] = -INFINITY;
+            }
             // P_q(j) goes to buffer j % 2, free once P_q(j-2) V has completed
             if (j >= 2) {
                 ok = __all_sync(0xffffffffu,
-                                mbar_wait_sleep(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag));
-                if (!ok) break;
+                                mbar_wait(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag));
+                if (!ok) continue;
             }
             // p for 8 keys at a time, summed into 8 partial sums, rounded and
-            // stored: key chunk k8 of 8 keys goes to 16-byte slot
-            // (k8 % 8) ^ (row % 8) of the row's 128-byte line in swizzle atom k8 / 8
-            uint8_t* prow = smem + SMEM_P + (q * 2 + (j & 1)) * P_BYTES + row * 128;
+            // stored: key chunk c of 8 keys of the tile (c = 8 * half + k8)
+            // goes to 16-byte slot (c % 8) ^ (row % 8) of the row's 128-byte
+            // line in swizzle atom c / 8 = half
+            uint8_t* prow = smem + SMEM_P + (q * 2 + (j & 1)) * P_BYTES + half * TILE_BYTES + row * 128;
             float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int k8 = 0; k8 < TK / 8; k8++) {
+            for (int k8 = 0; k8 < HK / 8; k8++) {
                 float p[8];
 #pragma unroll
-                for (int k = 0; k < 8; k++) {  // half on the SFU, half on the FMA pipe
-                    const float a = fmaf(sv[8 * k8 + k], sl2, -u);
-                    p[k] = k < 4 ? ex2f(a) : ex2_fma(a);
+                for (int k = 0; k < 8; k++) {
+                    p[k] = ex2f(fmaf(sv[8 * k8 + k], sl2, -u));
                     ps[k] += p[k];
                 }
                 uint4 v;
@@ -328,23 +363,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 v.y = pack16<T>(p[2], p[3]);
                 v.z = pack16<T>(p[4], p[5]);
                 v.w = pack16<T>(p[6], p[7]);
-                *reinterpret_cast<uint4*>(prow + (k8 >> 3) * TILE_BYTES + (((k8 & 7) ^ (row & 7)) << 4)) = v;
+                *reinterpret_cast<uint4*>(prow + ((k8 ^ (row & 7)) << 4)) = v;
             }
             l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             if (rescale) {
                 // O_q holds P V up to tile j-1 once that MMA has completed
-                ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar->o_full[q], (j - 1) & 1, err, abort_flag));
-                if (!ok) break;
+                ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_full[q], (j - 1) & 1, err, abort_flag));
+                if (!ok) continue;
                 tc_fence_after();
+                uint32_t r[32];
+                tmem_ld32(t_o, r);
+                tc_wait_ld();
 #pragma unroll
-                for (int c = 0; c < HD; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_o + c, r);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                    tmem_st32(t_o + c, r);
-                }
+                for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                tmem_st32(t_o, r);
                 tc_wait_st();
             }
             fence_proxy_async();
@@ -353,26 +385,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // never two phases ahead of its waiter.
             if (j >= 1) {
                 ok = __all_sync(0xffffffffu,
-                                mbar_wait_sleep(&bar->p_free[q][(j - 1) & 1], ((j - 1) >> 1) & 1, err, abort_flag));
-                if (!ok) break;
+                                mbar_wait(&bar->p_free[q][(j - 1) & 1], ((j - 1) >> 1) & 1, err, abort_flag));
+                if (!ok) continue;
             }
             tc_fence_before();
             mbar_arrive(&bar->p_full[q]);
         }
+        // the row sum: this half's and the other half's (every thread of the
+        // tile reaches this barrier, an aborted one too)
+        if (q < nq) {
+            const uint32_t xc = tmem + lanes + X_COL + (((nkt & 1) * 2 + q) * 2);
+            tmem_st1(xc + half, __float_as_uint(l));
+            tc_wait_st();
+            tc_fence_before();
+            tile_sync(q);
+            tc_fence_after();
+            l += __uint_as_float(tmem_ld1(xc + (half ^ 1)));
+            tc_wait_ld();
+        }
         if (ok) {
             // O_q is complete once the last P V has
-            ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar->o_full[q], (nkt - 1) & 1, err, abort_flag));
+            ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_full[q], (nkt - 1) & 1, err, abort_flag));
             if (ok) {
                 tc_fence_after();
-                float o[HD];
-#pragma unroll
-                for (int c = 0; c < HD; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
+                float o[32];
+                tmem_ld32(t_o, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
                 tc_wait_ld();
                 if (qi < L) {
                     const float inv = 1.0f / l;
-                    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)(start + qi) * D + h * HD);
+                    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)(start + qi) * D + h * HD + half * (HD / 2));
 #pragma unroll
-                    for (int c = 0; c < HD / 8; c++) {
+                    for (int c = 0; c < 4; c++) {
                         uint4 v;
                         v.x = pack16<T>(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
                         v.y = pack16<T>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
@@ -388,7 +431,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 9) tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == 17) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 }  // namespace

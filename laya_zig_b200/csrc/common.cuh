@@ -96,36 +96,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     }
 }
 
-// try_wait with a suspend-time hint: the thread sleeps until the phase
-// completes or about `ns` nanoseconds pass, instead of spinning.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-        : "memory");
-    return ok != 0;
-}
-
-// mbar_wait with the thread asleep between polls (20 us hint); same bound
-// and abort semantics.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err, volatile int* abort) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer();
-    while (true) {
-        if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
-        if (*abort) return false;
-        if (globaltimer() - t0 > WAIT_LIMIT_NS) {
-            atomicOr(err, ERR_WAIT_TIMEOUT);
-            *abort = 1;
-            return false;
-        }
-    }
-}
-
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
     asm volatile(
@@ -232,6 +202,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// One 32-bit column of the warp's 32 lanes (thread t: row lane base + t).
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    return r;
+}
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
 
 // 32 lanes x 16 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {

@@ -79,29 +79,3 @@ def test_tiles_per_block_at_the_bench_length():
             n += (khi + KB - 1) // KB - klo // KB
         return n
     assert tiles(180, 64) == 7 and tiles(180, -1) == 9
-
-
-def test_fma_pipe_exp2_restatement():
-    """attention_tc.cu computes half of the softmax's 2^x on the FMA pipe:
-    round to the nearest integer n by adding and subtracting 1.5 * 2^23,
-    2^f (|f| <= 1/2) by its degree-4 Taylor series in f ln 2, n added to the
-    exponent field. Restated here in float32 numpy: relative error under
-    6e-5 (P is then rounded to 16 bits, 2^-9 in bf16) over the range the
-    softmax uses, and a clamped -inf gives a value below 3e-38."""
-    import numpy as np
-    f32 = np.float32
-    x = np.concatenate([np.linspace(-125, 8, 200001, dtype=np.float32),
-                        np.array([-np.inf, -1e30, -0.5, 0.5, 0.0, 8.0], np.float32)])
-    xc = np.maximum(x, f32(-125.0))
-    t = (xc + f32(12582912.0)).astype(np.float32)
-    fr = (xc - (t - f32(12582912.0))).astype(np.float32)
-    p = f32(9.618129107628477e-3)
-    for c in (5.550410866482158e-2, 2.402265069591007e-1, 6.931471805599453e-1, 1.0):
-        p = (p * fr + f32(c)).astype(np.float32)
-    bits = (p.view(np.int32) + (t.view(np.int32) << np.int32(23))).astype(np.int32)
-    got = bits.view(np.float32).astype(np.float64)
-    assert np.all(np.abs(fr) <= 0.5)
-    finite = x > -125
-    ref = np.exp2(x[finite].astype(np.float64))
-    assert np.max(np.abs(got[finite] - ref) / ref) < 6e-5
-    assert got[~finite].max() < 3e-38
