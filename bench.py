@@ -20,6 +20,7 @@ Other workloads (not the headline line):
   --workload gemm    the four projection shapes at M = 180 and M = 11,520, each
                      launch timed alone (the reference's --benchgemm)
   --workload long    one 8,192-token decision (latency, attention roofline)
+  --workload single  one decision per call (the --serve / --snake latency)
 
 Kernel times in the rooflines: a CUDA graph of one forward with an event pair
 around every launch gives each launch's time; the event nodes stop
@@ -528,6 +529,62 @@ def run_long(args):
     model.close()
 
 
+def run_single(args):
+    """--workload single: the latency of one decision, the --serve / --snake
+    case of the reference (one forward per request): the C1 decision (64
+    tokens, 4 markers) and one Snake-style decision of 180 tokens (8
+    markers), each through the host call laya_gpu_forward (ids copied in,
+    logits/act/pooled copied out, one cached CUDA graph replayed) and as a
+    device-resident forward timed with CUDA events."""
+    import numpy as np
+    import torch
+    from laya_zig_b200 import gpu, synth
+    torch.cuda.set_device(0)
+    model = gpu.LayaGPU.from_bf16(synth.make_weights(0), device=0, precision=args.precision)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    steps = max(args.steps, 1)
+    rows = []
+    clocks = _clock_region(0)
+    clocks.start()
+    for name, d in (("C1 1x64, 4 markers", synth.parity_decision(1)), ("1x180, 8 markers", synth.snake_batch(1)[0])):
+        for _ in range(max(3, args.warmup)):
+            model.forward(d.ids, d.qtype, d.markers)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            model.forward(d.ids, d.qtype, d.markers)
+        host_ms = (time.perf_counter() - t0) * 1e3 / steps
+        p = gpu.pack([d])
+        dev = {k: torch.from_numpy(v.view(np.int32)).cuda() for k, v in p.items() if k != "max_len"}
+        G = int(p["cu_markers"][-1])
+        db = gpu.DeviceBatch(dev["ids"].data_ptr(), dev["cu_seqlens"].data_ptr(), dev["markers"].data_ptr(),
+                             dev["cu_markers"].data_ptr(), dev["qtypes"].data_ptr(), 1, len(p["ids"]), G, p["max_len"])
+        lg = torch.zeros(G, device="cuda")
+        ac = torch.zeros((1, 2), device="cuda")
+        for _ in range(3):
+            model.forward_device(db, lg.data_ptr(), ac.data_ptr(), stream=stream.cuda_stream)
+        model.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            model.forward_device(db, lg.data_ptr(), ac.data_ptr(), stream=stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        model.sync()
+        rows.append({"decision": name, "host_call_ms": host_ms, "device_ms": e0.elapsed_time(e1) / steps})
+    clk = clocks.stop()
+    model.close()
+    print(json.dumps({
+        "metric": "single-decision latency (host call laya_gpu_forward)", "value": rows[1]["host_call_ms"],
+        "unit": "ms", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup),
+        "ms_per_step": rows[1]["host_call_ms"], "higher_is_better": False, "scaling": "none", "vs_baseline": None,
+        "dtype": args.precision, "data": "synthetic (seeded weights and token ids)",
+        "config": {"workload": "one decision per call: C1 (64 tokens) and a 180-token Snake-style decision; "
+                               "consecutive calls, L2 not flushed (each call is a separate request)"},
+        "decisions": rows, "clocks": clk, "gpu_launches": 171 * steps * 4,
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -536,9 +593,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="snake", choices=["snake", "sweep", "gemm", "long"],
+    ap.add_argument("--workload", default="snake", choices=["snake", "sweep", "gemm", "long", "single"],
                     help="snake: the 64 x 180 headline batch (default); sweep: the bucketed throughput sweep; "
-                         "gemm: isolated projection GEMMs; long: one 8192-token decision")
+                         "gemm: isolated projection GEMMs; long: one 8192-token decision; "
+                         "single: one-decision latency")
     ap.add_argument("--sweep-n", type=int, default=65536)
     ap.add_argument("--long-len", type=int, default=8192, help="--workload long: the sequence length")
     args = ap.parse_args()
@@ -554,6 +612,9 @@ def main():
         return
     if args.workload == "long":
         run_long(args)
+        return
+    if args.workload == "single":
+        run_single(args)
         return
 
     import numpy as np
