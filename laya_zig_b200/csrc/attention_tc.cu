@@ -5,23 +5,19 @@
 // 128-row query tiles of one head of one sequence and streams the
 // sequence's keys and values through shared memory in tiles of 128:
 //
-//   warp 16     TMA producer: both Q tiles once, then K_j and V_j (128 x 64
+//   warp 8      TMA producer: both Q tiles once, then K_j and V_j (128 x 64
 //               16-bit boxes, 128-byte swizzle) into a KV_STAGES-deep ring.
-//   warp 17     TMEM owner and MMA issuer: S_q = Q_q K_j^T (M 128, N 128,
+//   warp 9      TMEM owner and MMA issuer: S_q = Q_q K_j^T (M 128, N 128,
 //               K 64) into TMEM, then O_q += P_q V_j (M 128, N 64, K 128)
 //               accumulated in TMEM across key tiles, with P from shared
 //               memory and V read MN-major.
-//   warps 0-15  softmax, eight warps per query tile: warps w and w + 4 of a
-//               tile's eight read the same TMEM lane quarter (query rows),
-//               the first the tile's keys 0-63, the second keys 64-127, so
-//               each thread holds half a row. Per key tile a thread copies
-//               its 64 scores from TMEM to registers (S_q is then free for
-//               the next tile's MMA), takes their maximum, exchanges it with
-//               its row's other half through shared memory, and writes
-//               p = 2^(s*log2(e)/8 - m*log2(e)/8) rounded to 16 bits into
-//               one of two P buffers (K-major swizzled, as the MMA reads it),
-//               keeping its half of the row sum in f32. Four softmax warps
-//               per scheduler hide each other's latencies.
+//   warps 0-7   two softmax warpgroups, one per query tile; thread t of a
+//               group owns query row t (its TMEM lane). Per key tile it
+//               copies its 128 scores from TMEM to registers (S_q is then
+//               free for the next tile's MMA), takes the row maximum, and
+//               writes p = 2^(s*log2(e)/8 - m*log2(e)/8) rounded to 16 bits
+//               into one of two P buffers (K-major swizzled, as the MMA
+//               reads it), keeping the row sum in f32.
 //
 // The reference point m of a row moves only when the row's maximum grows by
 // more than 8 in the exponent (p then stays below 2^8): the warp rescales
@@ -44,8 +40,7 @@ constexpr int TQ = 128;        // query rows per tile (one TMEM lane each)
 constexpr int TK = 128;        // keys per tile
 constexpr int NQT = 2;         // query tiles per CTA
 constexpr int KV_STAGES = 2;
-constexpr int TC_THREADS = 576;  // 16 softmax warps, producer, MMA issuer
-constexpr int SM_THREADS = 256;  // softmax threads per query tile
+constexpr int TC_THREADS = 320;
 constexpr int TILE_BYTES = TQ * HD * 2;            // 16 KB: a 128 x 64 16-bit box
 constexpr int P_BYTES = TQ * TK * 2;               // 32 KB: 128 x 128 16-bit, two 64-key swizzle atoms
 constexpr int SMEM_Q = 0;
@@ -54,11 +49,7 @@ constexpr int SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_P = SMEM_V + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_BAR = SMEM_P + 2 * NQT * P_BYTES;  // two P buffers per query tile
 constexpr int SMEM_TC = SMEM_BAR + 256 + 1024;     // barriers, TMEM slot, 1 KB alignment slack
-// TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384), then
-// the row halves' maxima and sums exchanged between the two warps of a lane
-// quarter at 384 + ((parity * 2 + q) * 2 + half)
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t X_COL = 384;
+constexpr uint32_t TMEM_COLS = 512;                // S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
 constexpr uint32_t IDESC_S_BF16 = idesc_f16(TQ, TK, true);
 constexpr uint32_t IDESC_S_F16 = idesc_f16(TQ, TK, false);
 // P . V: B (= V) is MN-major (head dim contiguous): transpose-B bit 16.
@@ -74,17 +65,16 @@ struct Bars {
     int abort;
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
-static_assert(SMEM_TC <= 227 * 1024, "shared memory");
 
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-    float d;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
+// Named barriers 1 and 2 pass a token between the two softmax warpgroups:
+// warpgroup q computes its exponentials only while it holds the token, so
+// the SFU serves one group at a time and each group's score loads and row
+// maxima overlap the other group's exponentials.
+__device__ __forceinline__ void token_wait(int q) {
+    asm volatile("bar.sync %0, 256;" ::"r"(1 + q) : "memory");
 }
-
-// barrier over the 256 softmax threads of query tile q (ids 1 and 2)
-__device__ __forceinline__ void tile_sync(int q) {
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + q), "n"(SM_THREADS) : "memory");
+__device__ __forceinline__ void token_pass(int q) {
+    asm volatile("bar.arrive %0, 256;" ::"r"(2 - q) : "memory");
 }
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -146,8 +136,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int q = 0; q < NQT; q++) {
             mbar_init(&bar->s_full[q], 1);
-            mbar_init(&bar->s_free[q], SM_THREADS);
-            mbar_init(&bar->p_full[q], SM_THREADS);
+            mbar_init(&bar->s_free[q], TQ);
+            mbar_init(&bar->p_full[q], TQ);
             mbar_init(&bar->o_full[q], 1);
             mbar_init(&bar->p_free[q][0], 1);
             mbar_init(&bar->p_free[q][1], 1);
@@ -157,8 +147,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         fence_barrier_init();
         fence_proxy_async();
     }
-    if (warp == 16 && lane == 0) prefetch_tmap(&qkv_map);
-    if (warp == 17) {
+    if (warp == 8 && lane == 0) prefetch_tmap(&qkv_map);
+    if (warp == 9) {
         tmem_alloc(&bar->tmem, TMEM_COLS);
         tmem_relinquish();
     }
@@ -169,7 +159,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     griddep_launch();
     griddep_wait();  // qkv comes from the preceding projection
 
-    if (warp == 16) {
+    if (warp == 8) {
         // ---------------------------------------------------------- TMA producer
         if (lane == 0) {
             int issued_phase[KV_STAGES];
@@ -193,7 +183,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (issued_phase[s] >= 0) drain_wait(&bar->kv_full[s], (uint32_t)issued_phase[s], err);
         }
         __syncwarp();
-    } else if (warp == 17) {
+    } else if (warp == 9) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
             constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
@@ -256,127 +246,105 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
     } else {
         // ---------------------------------------------------------- softmax
-        const int q = warp >> 3;                 // query tile of this warp
-        const int quarter = warp & 3;            // TMEM lanes (query rows) this warp may read
-        const int half = (warp >> 2) & 1;        // which 64 keys of the tile / 32 columns of O
+        const int q = warp >> 2;                 // query tile of this warpgroup
+        const int quarter = warp & 3;            // TMEM lanes this warp may read
         const int row = quarter * 32 + lane;     // query row in the tile
         const int qi = q0 + q * TQ + row;        // query row in the sequence
-        const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-        const uint32_t t_s = tmem + lanes + q * TK + half * (TK / 2);
-        const uint32_t t_o = tmem + lanes + 2 * TK + q * HD + half * (HD / 2);
+        const uint32_t t_s = tmem + ((uint32_t)(quarter * 32) << 16) + q * TK;
+        const uint32_t t_o = tmem + ((uint32_t)(quarter * 32) << 16) + 2 * TK + q * HD;
         const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
         constexpr float RESCALE = 8.0f;                  // exponent growth that moves the reference point
-        constexpr int HK = TK / 2;                       // keys per thread per tile
         float m = -INFINITY, l = 0.f;
         bool ok = q < nq;
-        // Every softmax thread of the tile takes part in each tile_sync below,
-        // also after a failed wait (ok false: it then only keeps the barrier
-        // count), so a thread that gives up never leaves the others waiting.
+        // Both warpgroups run every tile's token_wait / token_pass, also
+        // after a failed wait (ok false) or without a query tile (q >= nq),
+        // so neither is ever left waiting for the other.
         for (int j = 0; j < nkt; j++) {
+            float sv[TK];
+            float u = 0.f, alpha = 1.0f;
+            bool rescale = false;
             if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->s_full[q], j & 1, err, abort_flag));
-            const int kend = L - j * TK - half * HK;  // keys of this half inside the sequence
-            float mh = -INFINITY;
             if (ok) {
-                // first read of this half's scores: their maximum
-                float sv[HK];
                 tc_fence_after();
-                tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-                tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-                tc_wait_ld();
-                if (kend < HK) {  // only the sequence's last tile is masked
 #pragma unroll
-                    for (int i = 0; i < HK; i++)
+                for (int c = 0; c < TK; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
+                tc_wait_ld();
+                tc_fence_before();
+                mbar_arrive(&bar->s_free[q]);  // S_q may be overwritten by the next tile's MMA
+                const int kend = L - j * TK;   // keys of this tile inside the sequence (>= 1)
+                if (kend < TK) {               // only the sequence's last tile is masked
+#pragma unroll
+                    for (int i = 0; i < TK; i++)
                         if (i >= kend) sv[i] = -INFINITY;
                 }
                 float t[8];
 #pragma unroll
-                for (int k = 0; k < 8; k++) t[k] = max3f(sv[k], sv[k + 8], sv[k + 16]);
+                for (int i = 0; i < 8; i++) t[i] = fmaxf(sv[i], sv[i + 8]);
 #pragma unroll
-                for (int i = 24; i < HK; i += 16)
+                for (int i = 16; i < TK; i += 8)
 #pragma unroll
-                    for (int k = 0; k < 8; k++) t[k] = max3f(t[k], sv[i + k], sv[i + 8 + k]);
-                mh = max3f(max3f(t[0], t[1], t[2]), max3f(t[3], t[4], t[5]), fmaxf(t[6], t[7]));
-            }
-            // the row's maximum: this half's and the other half's, through a
-            // TMEM column of the shared lane quarter (columns alternate with
-            // the tile's parity, so one is rewritten only after its reader
-            // passed the next barrier)
-            const uint32_t xc = tmem + lanes + X_COL + (((j & 1) * 2 + q) * 2);
-            tmem_st1(xc + half, __float_as_uint(mh));
-            tc_wait_st();
-            tc_fence_before();
-            tile_sync(q);
-            tc_fence_after();
-            const float mx = fmaxf(mh, __uint_as_float(tmem_ld1(xc + (half ^ 1))));
-            tc_wait_ld();
-            if (!ok) continue;
-            // move the reference point when the maximum grew by more than
-            // RESCALE in the exponent (always on the first tile); both halves
-            // of a row decide alike, and a warp rescales its 32 columns of O
-            // for its 32 rows together (TMEM access is per warp)
-            const bool need = (mx - m) * sl2 > RESCALE;
-            float alpha = 1.0f;
-            if (j == 0) {
-                m = mx;
-            } else if (need) {
-                alpha = ex2f((m - mx) * sl2);
-                m = mx;
-                l *= alpha;
-            }
-            const bool rescale = j > 0 && __any_sync(0xffffffffu, need);
-            const float u = m * sl2;
-            // second read of the scores (S_q is then free for the next
-            // tile's MMA): p, the row sum and P
-            float sv[HK];
-            tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-            tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-            tc_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&bar->s_free[q]);
-            if (kend < HK) {
-#pragma unroll
-                for (int i = 0; i < HK; i++)
-                    if (i >= kend) sv[i] = -INFINITY;
-            }
-            // P_q(j) goes to buffer j % 2, free once P_q(j-2) V has completed
-            if (j >= 2) {
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag));
-                if (!ok) continue;
-            }
-            // p for 8 keys at a time, summed into 8 partial sums, rounded and
-            // stored: key chunk c of 8 keys of the tile (c = 8 * half + k8)
-            // goes to 16-byte slot (c % 8) ^ (row % 8) of the row's 128-byte
-            // line in swizzle atom c / 8 = half
-            uint8_t* prow = smem + SMEM_P + (q * 2 + (j & 1)) * P_BYTES + half * TILE_BYTES + row * 128;
-            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int k8 = 0; k8 < HK / 8; k8++) {
-                float p[8];
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    p[k] = ex2f(fmaf(sv[8 * k8 + k], sl2, -u));
-                    ps[k] += p[k];
+                    for (int k = 0; k < 8; k++) t[k] = fmaxf(t[k], sv[i + k]);
+                const float mx =
+                    fmaxf(fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3])), fmaxf(fmaxf(t[4], t[5]), fmaxf(t[6], t[7])));
+                // move the reference point when the maximum grew by more than
+                // RESCALE in the exponent (always on the first tile); the warp
+                // rescales its rows of O together (TMEM access is per warp),
+                // after P is written
+                const bool need = (mx - m) * sl2 > RESCALE;
+                if (j == 0) {
+                    m = mx;
+                } else if (need) {
+                    alpha = ex2f((m - mx) * sl2);
+                    m = mx;
+                    l *= alpha;
                 }
-                uint4 v;
-                v.x = pack16<T>(p[0], p[1]);
-                v.y = pack16<T>(p[2], p[3]);
-                v.z = pack16<T>(p[4], p[5]);
-                v.w = pack16<T>(p[6], p[7]);
-                *reinterpret_cast<uint4*>(prow + ((k8 ^ (row & 7)) << 4)) = v;
+                rescale = j > 0 && __any_sync(0xffffffffu, need);
+                u = m * sl2;
+                // P_q(j) goes to buffer j % 2, free once P_q(j-2) V has completed
+                if (j >= 2)
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag));
             }
-            l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            if (q == 1 || j > 0) token_wait(q);  // group 0 starts with the token
+            if (ok) {
+                // p for 8 keys at a time, summed into 8 partial sums, rounded and
+                // stored: key chunk k8 of 8 keys goes to 16-byte slot
+                // (k8 % 8) ^ (row % 8) of the row's 128-byte line in swizzle atom k8 / 8
+                uint8_t* prow = smem + SMEM_P + (q * 2 + (j & 1)) * P_BYTES + row * 128;
+                float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int k8 = 0; k8 < TK / 8; k8++) {
+                    float p[8];
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        p[k] = ex2f(fmaf(sv[8 * k8 + k], sl2, -u));
+                        ps[k] += p[k];
+                    }
+                    uint4 v;
+                    v.x = pack16<T>(p[0], p[1]);
+                    v.y = pack16<T>(p[2], p[3]);
+                    v.z = pack16<T>(p[4], p[5]);
+                    v.w = pack16<T>(p[6], p[7]);
+                    *reinterpret_cast<uint4*>(prow + (k8 >> 3) * TILE_BYTES + (((k8 & 7) ^ (row & 7)) << 4)) = v;
+                }
+                l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            }
+            token_pass(q);
+            if (!ok) continue;
             if (rescale) {
                 // O_q holds P V up to tile j-1 once that MMA has completed
                 ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_full[q], (j - 1) & 1, err, abort_flag));
                 if (!ok) continue;
                 tc_fence_after();
-                uint32_t r[32];
-                tmem_ld32(t_o, r);
-                tc_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                tmem_st32(t_o, r);
+                for (int c = 0; c < HD; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_o + c, r);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                    tmem_st32(t_o + c, r);
+                }
                 tc_wait_st();
             }
             fence_proxy_async();
@@ -391,31 +359,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc_fence_before();
             mbar_arrive(&bar->p_full[q]);
         }
-        // the row sum: this half's and the other half's (every thread of the
-        // tile reaches this barrier, an aborted one too)
-        if (q < nq) {
-            const uint32_t xc = tmem + lanes + X_COL + (((nkt & 1) * 2 + q) * 2);
-            tmem_st1(xc + half, __float_as_uint(l));
-            tc_wait_st();
-            tc_fence_before();
-            tile_sync(q);
-            tc_fence_after();
-            l += __uint_as_float(tmem_ld1(xc + (half ^ 1)));
-            tc_wait_ld();
-        }
+        if (q == 0) token_wait(0);  // takes group 1's last token_pass
         if (ok) {
             // O_q is complete once the last P V has
             ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_full[q], (nkt - 1) & 1, err, abort_flag));
             if (ok) {
                 tc_fence_after();
-                float o[32];
-                tmem_ld32(t_o, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+                float o[HD];
+#pragma unroll
+                for (int c = 0; c < HD; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
                 tc_wait_ld();
                 if (qi < L) {
                     const float inv = 1.0f / l;
-                    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)(start + qi) * D + h * HD + half * (HD / 2));
+                    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)(start + qi) * D + h * HD);
 #pragma unroll
-                    for (int c = 0; c < 4; c++) {
+                    for (int c = 0; c < HD / 8; c++) {
                         uint4 v;
                         v.x = pack16<T>(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
                         v.y = pack16<T>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
@@ -431,7 +389,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 17) tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == 9) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 }  // namespace
