@@ -42,14 +42,13 @@ constexpr int NQT = 2;         // query tiles per CTA
 constexpr int KV_STAGES = 2;
 constexpr int TC_THREADS = 320;
 constexpr int TILE_BYTES = TQ * HD * 2;            // 16 KB: a 128 x 64 16-bit box
-constexpr int P_BYTES = TQ * TK * 2;               // 32 KB: 128 x 128 16-bit, two 64-key swizzle atoms
 constexpr int SMEM_Q = 0;
 constexpr int SMEM_K = SMEM_Q + NQT * TILE_BYTES;
 constexpr int SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
-constexpr int SMEM_P = SMEM_V + KV_STAGES * TILE_BYTES;
-constexpr int SMEM_BAR = SMEM_P + 2 * NQT * P_BYTES;  // two P buffers per query tile
+constexpr int SMEM_BAR = SMEM_V + KV_STAGES * TILE_BYTES;  // P lives in TMEM
 constexpr int SMEM_TC = SMEM_BAR + 256 + 1024;     // barriers, TMEM slot, 1 KB alignment slack
-constexpr uint32_t TMEM_COLS = 512;                // S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
+constexpr uint32_t TMEM_COLS = 512;  // S_0, S_1 [0,256), O_0, O_1 [256,384), P_0, P_1 [384,512)
+constexpr uint32_t P_COL = 384;
 constexpr uint32_t IDESC_S_BF16 = idesc_f16(TQ, TK, true);
 constexpr uint32_t IDESC_S_F16 = idesc_f16(TQ, TK, false);
 // P . V: B (= V) is MN-major (head dim contiguous): transpose-B bit 16.
@@ -59,7 +58,7 @@ constexpr uint32_t IDESC_O_F16 = idesc_f16(TQ, HD, false) | (1u << 16);
 struct Bars {
     uint64_t q_full;
     uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
-    uint64_t s_full[NQT], s_free[NQT], p_full[NQT], o_full[NQT], p_free[NQT][2];
+    uint64_t s_full[NQT], s_free[NQT], p_full[NQT], o_full[NQT];
     uint64_t drain;
     uint32_t tmem;
     int abort;
@@ -94,6 +93,21 @@ template <>
 __device__ __forceinline__ uint32_t pack16<__half>(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// P's rounding to 16 bits, two values packed. For bf16 on the integer pipe
+// (the SFU, which also converts, is busy with the exponentials): add half a
+// bf16 ulp and keep the high halves, round to nearest with ties away from
+// zero, for the non-negative finite p here; f16 by conversion.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_p(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack_p<__nv_bfloat16>(float a, float b) {
+    return __byte_perm(__float_as_uint(a) + 0x8000u, __float_as_uint(b) + 0x8000u, 0x7632);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_p<__half>(float a, float b) {
+    return pack16<__half>(a, b);
 }
 
 // Bounded wait for an mbarrier phase with no abort flag (teardown drains).
@@ -139,8 +153,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&bar->s_free[q], TQ);
             mbar_init(&bar->p_full[q], TQ);
             mbar_init(&bar->o_full[q], 1);
-            mbar_init(&bar->p_free[q][0], 1);
-            mbar_init(&bar->p_free[q][1], 1);
         }
         mbar_init(&bar->drain, 1);
         bar->abort = 0;
@@ -189,8 +201,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
             const uint32_t idesc_s = BF ? IDESC_S_BF16 : IDESC_S_F16;
             const uint32_t idesc_o = BF ? IDESC_O_BF16 : IDESC_O_F16;
-            const uint32_t sq = smem_u32(smem + SMEM_Q), sk = smem_u32(smem + SMEM_K), sv = smem_u32(smem + SMEM_V),
-                           sp = smem_u32(smem + SMEM_P);
+            const uint32_t sq = smem_u32(smem + SMEM_Q), sk = smem_u32(smem + SMEM_K), sv = smem_u32(smem + SMEM_V);
             auto issue_s = [&](int q, int j) {
                 const int s = j % KV_STAGES;
 #pragma unroll
@@ -201,15 +212,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             };
             // P: two 64-key K-major atoms of 16 KB, 32 bytes per 16-key step;
             // V: MN-major, 16 keys (2 KB) per step, 8-key groups 1 KB apart
+            // P_q from TMEM (16-bit pairs, 8 columns per 16 keys), V MN-major
+            // from shared memory, 16 keys (2 KB) per step
             auto issue_o = [&](int q, int j) {
                 const int s = j % KV_STAGES;
-                const uint32_t pb = sp + (q * 2 + (j & 1)) * P_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < TK / 16; ks++)
-                    tc_mma_f16(tmem + 2 * TK + q * HD, sw128_desc(pb + (ks >> 2) * TILE_BYTES) + 2 * (ks & 3),
-                               sw128_desc(sv + s * TILE_BYTES + ks * 2048), idesc_o, (j | ks) != 0);
+                    tc_mma_f16_ts(tmem + 2 * TK + q * HD, tmem + P_COL + q * (TK / 2) + ks * 8,
+                                  sw128_desc(sv + s * TILE_BYTES + ks * 2048), idesc_o, (j | ks) != 0);
                 tc_commit(&bar->o_full[q]);
-                tc_commit(&bar->p_free[q][j & 1]);
             };
             bool ok = mbar_wait(&bar->q_full, 0, err, abort_flag);
             if (ok) ok = mbar_wait(&bar->kv_full[0], 0, err, abort_flag);
@@ -300,64 +311,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 rescale = j > 0 && __any_sync(0xffffffffu, need);
                 u = m * sl2;
-                // P_q(j) goes to buffer j % 2, free once P_q(j-2) V has completed
-                if (j >= 2)
-                    ok = __all_sync(0xffffffffu,
-                                    mbar_wait(&bar->p_free[q][j & 1], ((j >> 1) - 1) & 1, err, abort_flag));
             }
             if (q == 1 || j > 0) token_wait(q);  // group 0 starts with the token
+            if (ok && j > 0) {
+                // P_q and O_q are free once P_q(j-1) V has completed (this is
+                // also what keeps p_full from running two phases ahead)
+                ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_full[q], (j - 1) & 1, err, abort_flag));
+                if (ok) tc_fence_after();
+            }
             if (ok) {
-                // p for 8 keys at a time, summed into 8 partial sums, rounded and
-                // stored: key chunk k8 of 8 keys goes to 16-byte slot
-                // (k8 % 8) ^ (row % 8) of the row's 128-byte line in swizzle atom k8 / 8
-                uint8_t* prow = smem + SMEM_P + (q * 2 + (j & 1)) * P_BYTES + row * 128;
+                // p, rounded to 16 bits in pairs, into P_q's 64 TMEM columns
+                // (column c: keys 2c and 2c + 1), with the row sum in f32
+                const uint32_t t_p = tmem + ((uint32_t)(quarter * 32) << 16) + P_COL + q * (TK / 2);
                 float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int k8 = 0; k8 < TK / 8; k8++) {
-                    float p[8];
+                for (int c4 = 0; c4 < 4; c4++) {
+                    uint32_t pk[16];
 #pragma unroll
-                    for (int k = 0; k < 8; k++) {
-                        p[k] = ex2f(fmaf(sv[8 * k8 + k], sl2, -u));
-                        ps[k] += p[k];
+                    for (int i = 0; i < 16; i++) {
+                        const float a = ex2f(fmaf(sv[32 * c4 + 2 * i], sl2, -u));
+                        const float b = ex2f(fmaf(sv[32 * c4 + 2 * i + 1], sl2, -u));
+                        ps[(2 * i) & 7] += a;
+                        ps[(2 * i + 1) & 7] += b;
+                        pk[i] = pack_p<T>(a, b);
                     }
-                    uint4 v;
-                    v.x = pack16<T>(p[0], p[1]);
-                    v.y = pack16<T>(p[2], p[3]);
-                    v.z = pack16<T>(p[4], p[5]);
-                    v.w = pack16<T>(p[6], p[7]);
-                    *reinterpret_cast<uint4*>(prow + (k8 >> 3) * TILE_BYTES + (((k8 & 7) ^ (row & 7)) << 4)) = v;
+                    tmem_st16(t_p + 16 * c4, pk);
                 }
                 l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-            }
-            token_pass(q);
-            if (!ok) continue;
-            if (rescale) {
-                // O_q holds P V up to tile j-1 once that MMA has completed
-                ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_full[q], (j - 1) & 1, err, abort_flag));
-                if (!ok) continue;
-                tc_fence_after();
+                if (rescale) {
 #pragma unroll
-                for (int c = 0; c < HD; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_o + c, r);
-                    tc_wait_ld();
+                    for (int c = 0; c < HD; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld32(t_o + c, r);
+                        tc_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                    tmem_st32(t_o + c, r);
+                        for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                        tmem_st32(t_o + c, r);
+                    }
                 }
                 tc_wait_st();
+                tc_fence_before();
+                mbar_arrive(&bar->p_full[q]);
             }
-            fence_proxy_async();
-            // Hand P_q(j) over only once P_q(j-1) V has completed: the MMA
-            // warp has then taken p_full's previous phase, so the barrier is
-            // never two phases ahead of its waiter.
-            if (j >= 1) {
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(&bar->p_free[q][(j - 1) & 1], ((j - 1) >> 1) & 1, err, abort_flag));
-                if (!ok) continue;
-            }
-            tc_fence_before();
-            mbar_arrive(&bar->p_full[q]);
+            token_pass(q);
         }
         if (q == 0) token_wait(0);  // takes group 1's last token_pass
         if (ok) {
