@@ -349,8 +349,31 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
         for (int kb = 0; kb < nk; kb++)
             for (int j = 0; j < BK / KSUB; j++) tma_prefetch_l2_2d(&b_map, kb * BK + j * KSUB, n0);
     }
-    // Set-up above overlaps the previous kernel's tail; operands and outputs
-    // are touched only after it has completed.
+    // The first ring stages' weight boxes are requested now as well: no
+    // kernel writes the weights, so their HBM latency overlaps the previous
+    // kernel's tail, and after the dependency wait only the activations
+    // (A) of those stages remain to load. The stages are fresh, so no
+    // empty-barrier wait is needed; each stage's full barrier is armed for
+    // its A and B bytes together.
+    const int pre = (warp == 0 && lane == 0 && unit < total) ? (nk < C::STAGES ? nk : C::STAGES) : 0;
+    if (pre) {
+        const int n0 = (unit % tiles_n) * BN + (int)rank * C::B_ROWS;
+        for (int kb = 0; kb < pre; kb++) {
+            uint8_t* sa = smem + kb * C::STAGE_BYTES;
+            if constexpr (PAIR) {
+                const uint32_t bar = mapa_shared(smem_u32(&full[kb]), 0);
+                if (leader) mbar_arrive_expect_tx(&full[kb], 2 * C::STAGE_BYTES);
+                for (int j = 0; j < BK / KSUB; j++)
+                    tma_load_2d_pair(sa + C::A_BYTES + j * C::B_ROWS * KSUB * 2, &b_map, bar, kb * BK + j * KSUB, n0);
+            } else {
+                mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+                for (int j = 0; j < BK / KSUB; j++)
+                    tma_load_2d(sa + C::A_BYTES + j * C::B_ROWS * KSUB * 2, &b_map, &full[kb], kb * BK + j * KSUB, n0);
+            }
+        }
+    }
+    // Set-up above overlaps the previous kernel's tail; activations and
+    // outputs are touched only after it has completed.
     griddep_launch();
     griddep_wait();
 
@@ -360,10 +383,29 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
             uint32_t phase = 0;
             int issued_phase[C::STAGES];
             for (int s = 0; s < C::STAGES; s++) issued_phase[s] = -1;
+            // the A boxes of the stages whose B boxes were requested above,
+            // unconditionally, so every armed stage completes
+            if (pre) {
+                const int m0 = (unit / tiles_n) * TILE_M + (int)rank * BM;
+                for (int kb = 0; kb < pre; kb++) {
+                    uint8_t* sa = smem + kb * C::STAGE_BYTES;
+                    if constexpr (PAIR) {
+                        const uint32_t bar = mapa_shared(smem_u32(&full[kb]), 0);
+                        for (int j = 0; j < BK / KSUB; j++)
+                            tma_load_2d_pair(sa + j * BM * KSUB * 2, &a_map, bar, kb * BK + j * KSUB, m0);
+                    } else {
+                        for (int j = 0; j < BK / KSUB; j++)
+                            tma_load_2d(sa + j * BM * KSUB * 2, &a_map, &full[kb], kb * BK + j * KSUB, m0);
+                    }
+                    issued_phase[kb] = 0;
+                }
+                stage = pre % C::STAGES;
+                phase = pre == C::STAGES ? 1u : 0u;
+            }
             for (int t = unit; t < total && !*abort_flag; t += units) {
                 const int m0 = (t / tiles_n) * TILE_M + (int)rank * BM;
                 const int n0 = (t % tiles_n) * BN + (int)rank * C::B_ROWS;
-                for (int kb = 0; kb < nk; kb++) {
+                for (int kb = t == unit ? pre : 0; kb < nk; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, args.err, abort_flag)) goto producer_done;
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
                     if constexpr (PAIR) {
