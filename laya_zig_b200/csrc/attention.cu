@@ -7,10 +7,14 @@
 // warps hold 16 rows each. Scores and P.V run on the tensor cores
 // (mma.sync m16n8k16, f32 accumulate); the softmax is the online
 // (running max / running sum) form in f32 with exp2, normalised once at the
-// end as the reference does (2479-2486). Key/value tiles of 64 keys stream
-// through a 3-deep ring in swizzled shared memory with cp.async; the
-// prologue requests Q and the first three tiles at once, which is every tile
-// a 64-row block of a sequence of up to 192 tokens needs.
+// end as the reference does (2479-2486). Q and the key/value tiles of 64
+// keys arrive by TMA (one thread issues cp.async.bulk.tensor boxes of 64
+// rows x 128 bytes; the 128-byte swizzle is the XOR layout the ldmatrix
+// addressing below reads) into a 3-deep ring, each slot completing on its
+// own mbarrier; the prologue requests Q and the first three tiles at once,
+// which is every tile a 64-row block of a sequence of up to 192 tokens
+// needs. Rows past the sequence end hold the next sequence's keys (masked
+// below) or, past the batch, the TMA's zero fill.
 //
 // Inputs come straight from the QKV projection's output: row r of `qkv`
 // holds q | k | v (each 12 heads x 64, RoPE already applied to q and k),
@@ -24,7 +28,9 @@ constexpr int QB = 64;   // query rows per CTA
 constexpr int KB = 64;   // keys per tile
 constexpr int NST = 3;   // key/value tiles in flight
 constexpr int THREADS = 128;
-constexpr int SMEM_BYTES = (QB + 2 * NST * KB) * 64 * 2;  // 56 KB
+constexpr int TILE_BYTES = KB * 64 * 2;                            // 8 KB: 64 rows x 64 16-bit
+constexpr int BAR_OFFSET = (QB + 2 * NST * KB) * 64 * 2;               // 56 KB of tiles
+constexpr int SMEM_BYTES = BAR_OFFSET + 64 + 1024;                     // barriers, 1 KB alignment slack
 
 // element offset of (row, col) in a 64x64 16-bit tile whose 16-byte chunks
 // are XOR-swizzled by row, so ldmatrix row fetches never share a bank.
@@ -36,16 +42,6 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-    const int sz = valid ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(sz) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
@@ -92,28 +88,19 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Copy rows [r0, r0+64) x cols [c0, c0+64) of the [*, ld] matrix at `src`
-// into a swizzled tile; rows at or past `rend` are zero-filled.
 template <typename T>
-__device__ __forceinline__ void load_tile(T* tile, const T* src, int ld, int r0, int rend, int c0) {
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int ch = threadIdx.x + i * THREADS;
-        const int r = ch >> 3, cc = (ch & 7) * 8;
-        const bool valid = r0 + r < rend;
-        const T* s = src + (size_t)(valid ? r0 + r : r0) * ld + c0 + cc;
-        cp_async16(tile + swz(r, cc), s, valid);
-    }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
-                                                            const int* __restrict__ cu_seqlens, int M, int max_len,
-                                                            int window, int* err, int long_len) {
-    extern __shared__ __align__(128) uint8_t att_smem[];  // Q tile, then NST K tiles, then NST V tiles
-    T* sQ = reinterpret_cast<T*>(att_smem);
+__global__ void __launch_bounds__(THREADS, 3) attention_kernel(const __grid_constant__ CUtensorMap qkv_map,
+                                                            T* __restrict__ out, const int* __restrict__ cu_seqlens,
+                                                            int M, int max_len, int window, int* err, int long_len) {
+    // Q tile, then NST K tiles, then NST V tiles, 1 KB aligned (the TMA
+    // swizzle pattern is anchored to 1 KB); then the slots' barriers
+    extern __shared__ uint8_t att_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(att_smem_raw) + 1023) & ~uintptr_t(1023));
+    T* sQ = reinterpret_cast<T*>(smem);
     T* sK = sQ + QB * 64;
     T* sV = sK + NST * KB * 64;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + BAR_OFFSET);  // [0] Q, [1 + slot] K/V
+    __shared__ int abort_flag;
 
     griddep_launch();
     const int seq = blockIdx.z, h = blockIdx.y;
@@ -128,9 +115,14 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
     }
     const int q0 = blockIdx.x * QB;
     if (q0 >= L || L >= long_len) return;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i <= NST; i++) mbar_init(&bar[i], 1);
+        abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&qkv_map);
+    }
+    __syncthreads();
     griddep_wait();  // qkv comes from the preceding projection
-    const int ld = 3 * D;
-    const T* base = qkv + (size_t)start * ld;
 
     int klo = 0, khi = L;
     if (window >= 0) {
@@ -141,16 +133,21 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Prologue: Q and the first NST key/value tiles all requested at once
-    // (a 64-row block of a <= 192-token sequence needs at most 3), one
-    // commit group per tile so each can be waited for on its own.
-    load_tile(sQ, base, ld, q0, L, h * HD);
+    // (a 64-row block of a <= 192-token sequence needs at most 3).
+    int issued[NST];  // thread 0: phase of each slot's last request, -1 if none
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar[0], TILE_BYTES);
+        tma_load_2d(sQ, &qkv_map, &bar[0], h * HD, start + q0);
 #pragma unroll
-    for (int i = 0; i < NST; i++) {
-        if (kt0 + i < kt1) {
-            load_tile(sK + i * KB * 64, base, ld, (kt0 + i) * KB, L, D + h * HD);
-            load_tile(sV + i * KB * 64, base, ld, (kt0 + i) * KB, L, 2 * D + h * HD);
+        for (int i = 0; i < NST; i++) {
+            issued[i] = -1;
+            if (kt0 + i < kt1) {
+                mbar_arrive_expect_tx(&bar[1 + i], 2 * TILE_BYTES);
+                tma_load_2d(sK + i * KB * 64, &qkv_map, &bar[1 + i], D + h * HD, start + (kt0 + i) * KB);
+                tma_load_2d(sV + i * KB * 64, &qkv_map, &bar[1 + i], 2 * D + h * HD, start + (kt0 + i) * KB);
+                issued[i] = 0;
+            }
         }
-        cp_commit();
     }
 
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
@@ -161,11 +158,15 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
     for (int j = 0; j < 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     uint32_t qa[4][4];
 
+    bool ok = true;
     for (int kt = kt0; kt < kt1; kt++) {
         const int slot = (kt - kt0) % NST;
-        // NST + (kt - kt0) groups are committed; tile kt's is the oldest pending
-        cp_wait<NST - 1>();
-        __syncthreads();
+        ok = mbar_wait(&bar[1 + slot], ((kt - kt0) / NST) & 1, err, &abort_flag);
+        if (kt == kt0 && ok) ok = mbar_wait(&bar[0], 0, err, &abort_flag);
+        if (__syncthreads_or(!ok)) {  // every thread leaves together
+            ok = false;
+            break;
+        }
         if (kt == kt0) {
 #pragma unroll
             for (int ks = 0; ks < 4; ks++) {
@@ -284,11 +285,26 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
             }
         }
         __syncthreads();  // every warp is done with this slot before it is refilled
-        if (kt + NST < kt1) {
-            load_tile(sK + slot * KB * 64, base, ld, (kt + NST) * KB, L, D + h * HD);
-            load_tile(sV + slot * KB * 64, base, ld, (kt + NST) * KB, L, 2 * D + h * HD);
+        if (threadIdx.x == 0 && kt + NST < kt1) {
+            mbar_arrive_expect_tx(&bar[1 + slot], 2 * TILE_BYTES);
+            tma_load_2d(sK + slot * KB * 64, &qkv_map, &bar[1 + slot], D + h * HD, start + (kt + NST) * KB);
+            tma_load_2d(sV + slot * KB * 64, &qkv_map, &bar[1 + slot], 2 * D + h * HD, start + (kt + NST) * KB);
+            issued[slot] = ((kt + NST - kt0) / NST) & 1;
         }
-        cp_commit();  // possibly empty: keeps one group per tile
+    }
+    if (!ok) {
+        // a wait gave up: every box requested lands before the CTA (and its
+        // shared memory) goes away; nothing is stored
+        if (threadIdx.x == 0) {
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try_wait(&bar[0], 0) && globaltimer() - t0 < WAIT_LIMIT_NS) {
+            }
+            for (int i = 0; i < NST; i++)
+                if (issued[i] >= 0)
+                    while (!mbar_try_wait(&bar[1 + i], (uint32_t)issued[i]) && globaltimer() - t0 < WAIT_LIMIT_NS) {
+                    }
+        }
+        return;
     }
 
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -306,16 +322,15 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const T* __restri
 
 }  // namespace
 
-cudaError_t launch_attention(bool bf16, const void* qkv, void* out, const int* cu_seqlens, int n_seqs, int M,
-                             int max_len, int window, int* err, cudaStream_t stream, int long_len) {
+cudaError_t launch_attention(bool bf16, const CUtensorMap& qkv_map, void* out, const int* cu_seqlens, int n_seqs,
+                             int M, int max_len, int window, int* err, cudaStream_t stream, int long_len) {
     if (n_seqs <= 0 || max_len <= 0) return cudaSuccess;
     dim3 grid((max_len + QB - 1) / QB, H, n_seqs);
     if (bf16)
-        return launch_k(attention_kernel<__nv_bfloat16>, grid, THREADS, SMEM_BYTES, stream,
-                        static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), cu_seqlens, M,
-                        max_len, window, err, long_len);
-    return launch_k(attention_kernel<__half>, grid, THREADS, SMEM_BYTES, stream, static_cast<const __half*>(qkv),
-                    static_cast<__half*>(out), cu_seqlens, M, max_len, window, err, long_len);
+        return launch_k(attention_kernel<__nv_bfloat16>, grid, THREADS, SMEM_BYTES, stream, qkv_map,
+                        static_cast<__nv_bfloat16*>(out), cu_seqlens, M, max_len, window, err, long_len);
+    return launch_k(attention_kernel<__half>, grid, THREADS, SMEM_BYTES, stream, qkv_map, static_cast<__half*>(out),
+                    cu_seqlens, M, max_len, window, err, long_len);
 }
 
 int attention_tc_min_len() {

@@ -264,6 +264,7 @@ struct ActMaps {
     CUtensorMap a_xn, a_ctx, a_mlp, a_ff;  // A operands, box 128 x 64
     CUtensorMap o_qkv, o_mlp, o_ff, o_x;   // outputs, box 32 rows x 128 bytes
     CUtensorMap a_qkv;                     // tcgen05 attention's Q, K, V boxes, 128 x 64
+    CUtensorMap a_qkv64;                   // mma.sync attention's Q, K, V boxes, 64 x 64
 };
 
 int build_maps(laya_ctx* c, int M, ActMaps* m) {
@@ -276,6 +277,7 @@ int build_maps(laya_ctx* c, int M, ActMaps* m) {
     if (r == CUDA_SUCCESS) r = make_out_map(&m->o_ff, c->ff, HEAD_FF, M, 2, c->bf16);
     if (r == CUDA_SUCCESS) r = make_out_map(&m->o_x, c->x, D, M, 4, c->bf16);
     if (r == CUDA_SUCCESS) r = make_tmap_2d(&m->a_qkv, c->qkv, 3 * D, M, 128, c->bf16);
+    if (r == CUDA_SUCCESS) r = make_tmap_2d(&m->a_qkv64, c->qkv, 3 * D, M, 64, c->bf16);
     if (r != CUDA_SUCCESS) return fail(c, LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return LAYA_OK;
 }
@@ -301,7 +303,7 @@ cudaError_t gemm(laya_ctx* c, int epi, const CUtensorMap& a, const CUtensorMap& 
 cudaError_t attention(laya_ctx* c, const Batch& b, const ActMaps& am, int window, cudaStream_t s) {
     const int tc_len = attention_tc_min_len();
     const bool tc = window < 0 && b.maxlen >= tc_len;
-    cudaError_t e = launch_attention(c->bf16, c->qkv, c->ctxb, b.cu, b.S, b.M, b.maxlen, window, c->d_err, s,
+    cudaError_t e = launch_attention(c->bf16, am.a_qkv64, c->ctxb, b.cu, b.S, b.M, b.maxlen, window, c->d_err, s,
                                      tc ? tc_len : 0x7fffffff);
     if (e == cudaSuccess && tc)
         e = launch_attention_tc(c->bf16, am.a_qkv, c->ctxb, b.cu, b.S, b.M, b.maxlen, tc_len, c->d_err, s);
