@@ -111,10 +111,14 @@ __global__ void __launch_bounds__(THREADS, 3) attention_kernel(const __grid_cons
     // is flagged and left alone, so no row outside the batch is touched.
     if (start < 0 || L < 0 || L > max_len || start > M - L) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_BAD_INDEX);
+        griddep_exit();
         return;
     }
     const int q0 = blockIdx.x * QB;
-    if (q0 >= L || L >= long_len) return;
+    if (q0 >= L || L >= long_len) {  // past the sequence end, or the tcgen05 kernel's sequence
+        griddep_exit();
+        return;
+    }
     if (threadIdx.x == 0) {
         for (int i = 0; i <= NST; i++) mbar_init(&bar[i], 1);
         abort_flag = 0;

@@ -135,10 +135,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int L = cu_seqlens[seq + 1] - start;
     if (start < 0 || L < 0 || L > max_len || start > M - L) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_BAD_INDEX);
+        griddep_exit();
         return;
     }
     const int q0 = blockIdx.x * (NQT * TQ);
-    if (L < min_len || q0 >= L) return;  // shorter sequences are the mma.sync kernel's
+    if (L < min_len || q0 >= L) {  // shorter sequences are the mma.sync kernel's
+        griddep_exit();
+        return;
+    }
     const int nq = min(NQT, (L - q0 + TQ - 1) / TQ);  // query tiles with rows in the sequence
     const int nkt = (L + TK - 1) / TK;
 

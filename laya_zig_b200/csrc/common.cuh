@@ -336,9 +336,18 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t mask) {
 // calls griddep_wait() before touching anything an earlier kernel wrote or
 // will read. griddep_wait() returns once the predecessor has completed and
 // its writes are visible; since that predecessor waited the same way, every
-// earlier kernel has completed too. Launched without the attribute, both
-// calls are no-ops.
+// earlier kernel has completed too. That chain holds only if every grid has
+// at least one block that waits: a block that leaves early without work
+// calls griddep_exit(), never a bare return. Launched without the attribute,
+// these calls are no-ops.
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Leave a block that has no work. Block (0, 0, 0) waits for the predecessor
+// first, so the grid cannot complete before it, even when every block of the
+// grid leaves early (a batch whose sequences all go to another kernel); the
+// other blocks leave at once.
+__device__ __forceinline__ void griddep_exit() {
+    if ((blockIdx.x | blockIdx.y | blockIdx.z) == 0) griddep_wait();
+}
 // Let the next kernel in the stream start launching (its CTAs still wait in
 // griddep_wait until this grid completes).
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -7,6 +7,10 @@
   largest bucket of the sweep). Checked by size-independent properties: each
   sequence's results are bit-identical to its own single-sequence pass (the
   packing never mixes sequences), and a sample matches the oracle.
+* Around the tcgen05 attention threshold: 2,047-2,300-token sequences in
+  one batch with a short one, each bit-identical to its own single pass
+  (where every block of the mma.sync grid has no work) and checked against
+  the oracle.
 """
 import numpy as np
 import pytest
@@ -53,3 +57,27 @@ def test_full_bucket_packing_invariance(gpu_model, oracle_model):
         r = oracle_model.forward(d.ids, d.markers, d.qtype)
         assert row_rel(outs[j].pooled, r["pooled"]) <= 2e-2
         assert np.abs(outs[j].act - r["act"]).max() <= 1e-3
+
+
+def test_long_batch_threshold_and_ragged_tiles(gpu_model, oracle_model):
+    """Sequences around the tcgen05 kernel's threshold in one batch with a
+    short one: 2,047 tokens (mma.sync), 2,048 (tcgen05, whole key tiles),
+    2,049 (tcgen05, a last key tile of one key and a last query tile of one
+    row), 2,300 (partial tiles). Each against the oracle, and each
+    bit-identical to its own single-sequence pass: the kernel is chosen per
+    sequence, never per batch."""
+    from laya_zig_b200 import gpu, synth
+    rng = np.random.Generator(np.random.PCG64(41))
+    batch = [synth._decision(rng, L, sorted(rng.choice(np.arange(1, L - 1), 4, replace=False).tolist()), L % 3,
+                             option_tokens=True)
+             for L in (300, 2047, 2048, 2049, 2300)]
+    outs = gpu_model.forward_batch(batch, want_pooled=True, want_hidden=True)
+    for d, g in zip(batch, outs):
+        s = gpu_model.forward(d.ids, d.qtype, d.markers)
+        np.testing.assert_array_equal(s.logits, g.logits)
+        np.testing.assert_array_equal(s.act, g.act)
+        np.testing.assert_array_equal(s.pooled, g.pooled)
+        r = oracle_model.forward(d.ids, d.markers, d.qtype, want_hidden=True)
+        assert row_rel(g.hidden, r["hidden"]) <= 2e-2, len(d.ids)
+        assert np.abs(gpu.option_probs(g.logits, 0) - gpu.option_probs(r["logits"], 0)).max() <= 1e-3
+        assert np.abs(g.act - r["act"]).max() <= 1e-3
