@@ -252,7 +252,9 @@ LAYA_API int laya_gpu_decision_tail_noalloc(laya_ctx* ctx, const float* hidden, 
 /* One projection, device pointers: out[M][N] (f32) = x[M][K] . w[N][K]^T
  * (+ bias[N]); x and w 16-bit of `elem_dtype` (LAYA_DT_BF16 or LAYA_DT_F16).
  * N a multiple of 128, K a multiple of 128; device pointers 16-byte aligned.
- * Runs on `stream` (NULL = default stream) of the current device. */
+ * Runs on `stream` (NULL = default stream) of the current device, ordered
+ * after the work before it on that stream: x, w and bias may come from the
+ * kernel just before. */
 LAYA_API int laya_gpu_linear(const void* x, const void* w, const float* bias, float* out, int M, int N, int K,
                     int elem_dtype, void* stream);
 

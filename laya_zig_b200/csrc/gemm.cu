@@ -337,11 +337,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // The weights (B) do not depend on the previous kernel. When every CTA
-    // (pair) has at most one tile (small M: a few SMs stream each
-    // projection's weights), the producer asks for its tile's B boxes in L2
-    // now, so their HBM latency overlaps the previous kernel's tail
-    // (single decisions 2.6-3% faster). With more tiles than CTAs the
+    // When every CTA (pair) has at most one tile (small M: a few SMs stream
+    // each projection's weights), the producer asks for its tile's B boxes
+    // in L2 now, so their HBM latency overlaps the previous kernel's tail
+    // (single decisions 2.6-3% faster). This is only a hint: L2 is
+    // coherent, so a B that the previous kernel still writes is read
+    // correctly after the wait. With more tiles than CTAs the
     // prefetched boxes only displace live activations from L2 (0.8% slower
     // on a 64 x 180 batch), so there is none.
     if (warp == 0 && lane == 0 && unit < total && total <= units) {
@@ -349,13 +350,15 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& a_map, const CUtens
         for (int kb = 0; kb < nk; kb++)
             for (int j = 0; j < BK / KSUB; j++) tma_prefetch_l2_2d(&b_map, kb * BK + j * KSUB, n0);
     }
-    // The first ring stages' weight boxes are requested now as well: no
-    // kernel writes the weights, so their HBM latency overlaps the previous
-    // kernel's tail, and after the dependency wait only the activations
-    // (A) of those stages remain to load. The stages are fresh, so no
-    // empty-barrier wait is needed; each stage's full barrier is armed for
-    // its A and B bytes together.
-    const int pre = (warp == 0 && lane == 0 && unit < total) ? (nk < C::STAGES ? nk : C::STAGES) : 0;
+    // The first ring stages' weight boxes are requested now as well when
+    // no kernel writes B (the context's weights; a caller's matrix may
+    // come from the kernel just before): their HBM latency overlaps the
+    // previous kernel's tail, and after the dependency wait only the
+    // activations (A) of those stages remain to load. The stages are
+    // fresh, so no empty-barrier wait is needed; each stage's full barrier
+    // is armed for its A and B bytes together.
+    const int pre =
+        (warp == 0 && lane == 0 && unit < total && args.b_const) ? (nk < C::STAGES ? nk : C::STAGES) : 0;
     if (pre) {
         const int n0 = (unit % tiles_n) * BN + (int)rank * C::B_ROWS;
         for (int kb = 0; kb < pre; kb++) {

@@ -25,6 +25,8 @@ struct GemmArgs {
     int rope_ld;
     int rope_cols;          // EPI_QKV: RoPE applies to columns [0, rope_cols)
     int* err;               // device error word
+    int b_const;            // 1: no kernel writes B (the context's weights), so its first
+                            // ring stages are loaded before the dependency wait
 };
 
 // 2-D tensor map over a row-major [rows][inner] 16-bit matrix, box

@@ -293,6 +293,7 @@ cudaError_t gemm(laya_ctx* c, int epi, const CUtensorMap& a, const CUtensorMap& 
     g.rope_ld = c->capM;
     g.rope_cols = rope_cols;
     g.err = c->d_err;
+    g.b_const = 1;  // B is one of the context's weights, written once at create
     return launch_gemm(epi, 256, c->bf16, a, b, out, g, c->num_sms, s);
 }
 
