@@ -376,16 +376,23 @@ def run_gemm(args):
     """--workload gemm: the projection shapes at M = 180 and 11,520 through
     laya_gpu_linear (the drop-in for linear16: bf16 operands, f32 out,
     tcgen05 cta_group::2 kernel), each launch timed alone with CUDA events on
-    its stream after an L2 flush; A ~ N(0, 1), W ~ N(0, 0.02), rounded to
-    bf16. Beside it, cuBLAS through torch.mm on the same operands (f32 out
-    where torch offers it). Every output is checked against an f64 product."""
+    its stream after an L2 flush that leaves no dirty lines (a write of a
+    buffer larger than L2, then a read of another one); A ~ N(0, 1), W ~
+    N(0, 0.02), rounded to bf16. Beside it, cuBLAS through torch.mm on the
+    same operands (f32 out where torch offers it). Every output is checked
+    against an f64 product."""
     import torch
     from laya_zig_b200 import gpu
     torch.cuda.set_device(0)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     sp = stream.cuda_stream
+    # L2 flush before every timed launch: a write of a buffer larger than L2
+    # evicts the operands, then a read of a second one evicts the first's
+    # dirty lines, so their write-back (as large as a launch's own traffic
+    # here) happens before the launch's start event, not inside it
     flush = torch.empty(flush_bytes(), dtype=torch.uint8, device="cuda")
+    flush_rd = torch.zeros(flush_bytes() // 4, dtype=torch.int32, device="cuda")
     gen = torch.Generator(device="cuda").manual_seed(7)
     steps, warm = max(args.steps, 1), max(args.warmup, 3)
 
@@ -395,6 +402,7 @@ def run_gemm(args):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         for a, b in ev:
             flush.zero_()
+            flush_rd.sum()
             a.record(stream)
             fn()
             b.record(stream)
@@ -439,7 +447,8 @@ def run_gemm(args):
         "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (A ~ N(0,1), W ~ N(0,0.02), bf16)",
         "config": {"workload": "isolated projection GEMMs through laya_gpu_linear (f32 out), M in {180, 11520}",
-                   "l2": "flushed before every timed launch (%d MB write)" % (flush_bytes() // 10**6),
+                   "l2": "flushed before every timed launch (%d MB write, then a %d MB read of another "
+                         "buffer: cold and clean)" % (flush_bytes() // 10**6, flush_bytes() // 10**6),
                    "time": "median of %d launches" % steps},
         "roofline": {"bound": "tensor", "achieved": fl / t / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": fl / t / 1e12 / peak, "traffic": None, "peak_source": peak_src,
