@@ -185,6 +185,9 @@ class LayaGPU:
         if rc != LAYA_OK:
             raise _error(rc, lib.laya_gpu_last_error(None).decode())
         self._h = h
+        # kept on the instance: at interpreter exit the module's `lib` may be
+        # cleared before a context that is still alive is collected
+        self._destroy = lib.laya_gpu_destroy
         self.device = device
         self.precision = precision
 
@@ -200,7 +203,7 @@ class LayaGPU:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib.laya_gpu_destroy(self._h)
+            self._destroy(self._h)
             self._h = None
 
     def __del__(self):
