@@ -107,3 +107,33 @@ def test_gemm_rejects_bad_shape():
     out = torch.zeros((64, 128), dtype=torch.float32, device="cuda")
     with pytest.raises(gpu.LayaError):
         gpu.linear(x.data_ptr(), w.data_ptr(), 0, out.data_ptr(), 64, 128, 100)
+
+
+def test_linear_after_a_kernel_that_writes_its_operands():
+    """x and w written by the kernel just before, on the same stream, each
+    call with new values: the projection is ordered after that kernel (its
+    weight boxes are not requested before the dependency wait, as the
+    forward's constant weights are)."""
+    import torch
+    from laya_zig_b200 import gpu
+    rng = np.random.default_rng(11)
+    M, N, K = 11520, 2304, 768
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        x = torch.empty((M, K), dtype=torch.bfloat16, device="cuda")
+        w = torch.empty((N, K), dtype=torch.bfloat16, device="cuda")
+        out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        for i in range(3):
+            xb = _rand_bits(rng, (M, K), 1.0)
+            wb = _rand_bits(rng, (N, K), 0.02)
+            xs = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+            ws = torch.from_numpy(wb.view(np.int16)).cuda().view(torch.bfloat16)
+            stream.synchronize()
+            # elementwise kernels (a copy may be a memcpy, which no launch
+            # overlaps) on `stream`, right before the projection; x 1 is exact
+            torch.mul(xs, 1.0, out=x)
+            torch.mul(ws, 1.0, out=w)
+            gpu.linear(x.data_ptr(), w.data_ptr(), 0, out.data_ptr(), M, N, K, "BF16", stream.cuda_stream)
+            stream.synchronize()
+            rel = _check(out.cpu().numpy(), _to_f64(xb), _to_f64(wb))
+            assert rel < 1e-4, (i, rel)
